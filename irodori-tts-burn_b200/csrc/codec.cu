@@ -1,0 +1,310 @@
+// DACVAE decoder (src/codec/decoder.rs:17-126, layers.rs:27-75,
+// bottleneck.rs:31-33, model.rs:60-65) on channel-major activations [B, C, T].
+//
+// conv1d: 64 output channels x 64 samples per CTA, Snake fused into the input
+//   staging (x + sin^2(a x) / (a + 1e-9), src/codec/layers.rs:27-33), bias,
+//   residual add and tanh fused into the output.
+// conv_transpose1d (kernel 2s, stride s, padding ceil(s/2)): polyphase -- each
+//   output sample receives exactly two taps per input channel.
+#include <map>
+
+#include "codec.hpp"
+#include "safetensors.hpp"
+
+namespace irt {
+
+namespace {
+
+constexpr int CO_T = 64, T_T = 64, CI_T = 16, MAXK = 7, MAXDIL = 9;
+constexpr int XW = T_T + (MAXK - 1) * MAXDIL;
+
+__device__ __forceinline__ float snake_f(float x, float a) {
+  float s = sinf(a * x);
+  return x + s * s / (a + 1e-9f);
+}
+
+__global__ void __launch_bounds__(256) conv1d_kernel(const float* __restrict__ x, int Cin, int T,
+                                                     const float* __restrict__ w, const float* __restrict__ bias,
+                                                     int Cout, int K, int dil, int pad,
+                                                     const float* __restrict__ alpha,
+                                                     const float* __restrict__ res, int tanh_out,
+                                                     float* __restrict__ y) {
+  __shared__ float xs[CI_T][XW];
+  __shared__ float wsm[CI_T][MAXK][CO_T];
+  const int b = blockIdx.z;
+  const int co0 = blockIdx.y * CO_T, t0 = blockIdx.x * T_T;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const int span = T_T + (K - 1) * dil;
+  float acc[4][4] = {};
+  const float* xb = x + (long)b * Cin * T;
+  for (int c0 = 0; c0 < Cin; c0 += CI_T) {
+    for (int e = threadIdx.x; e < CI_T * span; e += 256) {
+      int ci = e / span, j = e % span;
+      int gc = c0 + ci, gt = t0 - pad + j;
+      float v = 0.f;
+      if (gc < Cin && gt >= 0 && gt < T) {
+        v = xb[(long)gc * T + gt];
+        if (alpha) v = snake_f(v, alpha[gc]);
+      }
+      xs[ci][j] = v;
+    }
+    for (int e = threadIdx.x; e < CI_T * K * CO_T; e += 256) {
+      int co = e % CO_T, r = e / CO_T;
+      int k = r % K, ci = r / K;
+      int gco = co0 + co, gc = c0 + ci;
+      wsm[ci][k][co] = (gco < Cout && gc < Cin) ? w[((long)gco * Cin + gc) * K + k] : 0.f;
+    }
+    __syncthreads();
+    for (int ci = 0; ci < CI_T; ++ci) {
+      for (int k = 0; k < K; ++k) {
+        float xv[4], wv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xv[j] = xs[ci][tx + 16 * j + k * dil];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) wv[i] = wsm[ci][k][ty * 4 + i];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(wv[i], xv[j], acc[i][j]);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int co = co0 + ty * 4 + i;
+    if (co >= Cout) continue;
+    float bv = bias ? bias[co] : 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int t = t0 + tx + 16 * j;
+      if (t >= T) continue;
+      long idx = ((long)b * Cout + co) * T + t;
+      float v = acc[i][j] + bv;
+      if (res) v += res[idx];
+      if (tanh_out) v = tanhf(v);
+      y[idx] = v;
+    }
+  }
+}
+
+constexpr int CT_CI = 4, MAXS = 12;
+
+__global__ void __launch_bounds__(256) convt_kernel(const float* __restrict__ x, int Cin, int T,
+                                                    const float* __restrict__ w, const float* __restrict__ bias,
+                                                    int Cout, int stride, int pad, const float* __restrict__ alpha,
+                                                    float* __restrict__ y, int Tout) {
+  __shared__ float xs[CT_CI][T_T / 2 + 4];
+  __shared__ float wsm[CT_CI][2 * MAXS][CO_T];
+  const int b = blockIdx.z;
+  const int co0 = blockIdx.y * CO_T, t0 = blockIdx.x * T_T;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const int K = 2 * stride;
+  const int tin0 = (t0 + pad) / stride - 1;  // first input sample the tile touches
+  const int nin = (t0 + T_T - 1 + pad) / stride - tin0 + 1;
+  float acc[4][4] = {};
+  const float* xb = x + (long)b * Cin * T;
+  int qj[4], rj[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    int t = t0 + tx + 16 * j;
+    qj[j] = (t + pad) / stride;
+    rj[j] = (t + pad) % stride;
+  }
+  for (int c0 = 0; c0 < Cin; c0 += CT_CI) {
+    for (int e = threadIdx.x; e < CT_CI * nin; e += 256) {
+      int ci = e / nin, j = e % nin;
+      int gc = c0 + ci, gt = tin0 + j;
+      float v = 0.f;
+      if (gc < Cin && gt >= 0 && gt < T) {
+        v = xb[(long)gc * T + gt];
+        if (alpha) v = snake_f(v, alpha[gc]);
+      }
+      xs[ci][j] = v;
+    }
+    for (int e = threadIdx.x; e < CT_CI * K * CO_T; e += 256) {
+      int co = e % CO_T, r = e / CO_T;
+      int k = r % K, ci = r / K;
+      int gco = co0 + co, gc = c0 + ci;
+      wsm[ci][k][co] = (gco < Cout && gc < Cin) ? w[((long)gc * Cout + gco) * K + k] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int ci = 0; ci < CT_CI; ++ci) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float x0 = xs[ci][qj[j] - tin0];      // k = r
+        float x1 = xs[ci][qj[j] - 1 - tin0];  // k = r + s
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          acc[i][j] = fmaf(wsm[ci][rj[j]][ty * 4 + i], x0, fmaf(wsm[ci][rj[j] + stride][ty * 4 + i], x1, acc[i][j]));
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int co = co0 + ty * 4 + i;
+    if (co >= Cout) continue;
+    float bv = bias ? bias[co] : 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int t = t0 + tx + 16 * j;
+      if (t < Tout) y[((long)b * Cout + co) * Tout + t] = acc[i][j] + bv;
+    }
+  }
+}
+
+__global__ void transpose_kernel(const float* in, float* out, int B, int T, int C) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)B * T * C) return;
+  int c = (int)(i % C);
+  long r = i / C;
+  int t = (int)(r % T), b = (int)(r / T);
+  out[((long)b * C + c) * T + t] = in[i];
+}
+
+}  // namespace
+
+void conv1d(const float* x, int B, int Cin, int T, const float* w, const float* bias, int Cout, int K, int dil,
+            int pad, const float* snake_alpha, const float* residual, int tanh_out, float* y, cudaStream_t s) {
+  if (K > MAXK || (K - 1) * dil > (MAXK - 1) * MAXDIL) throw unsupported("conv1d kernel/dilation too large");
+  dim3 grid((T + T_T - 1) / T_T, (Cout + CO_T - 1) / CO_T, B);
+  conv1d_kernel<<<grid, 256, 0, s>>>(x, Cin, T, w, bias, Cout, K, dil, pad, snake_alpha, residual, tanh_out, y);
+  IRT_CHECK_LAUNCH();
+}
+
+void conv_transpose1d(const float* x, int B, int Cin, int T, const float* w, const float* bias, int Cout, int stride,
+                      int pad, const float* snake_alpha, float* y, int Tout, cudaStream_t s) {
+  if (stride > MAXS || stride < 1) throw unsupported("conv_transpose1d stride > 12");
+  dim3 grid((Tout + T_T - 1) / T_T, (Cout + CO_T - 1) / CO_T, B);
+  convt_kernel<<<grid, 256, 0, s>>>(x, Cin, T, w, bias, Cout, stride, pad, snake_alpha, y, Tout);
+  IRT_CHECK_LAUNCH();
+}
+
+void transpose_btc_bct(const float* in, float* out, int B, int T, int C, cudaStream_t s) {
+  long n = (long)B * T * C;
+  if (!n) return;
+  transpose_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(in, out, B, T, C);
+  IRT_CHECK_LAUNCH();
+}
+
+// ---------------------------------------------------------------------------
+// Codec object
+// ---------------------------------------------------------------------------
+
+namespace {
+void up_f32(DevBuf& dst, const TensorView& v) {
+  std::vector<float> h((size_t)v.numel());
+  decode_to_f32(v, h.data());
+  dst.alloc(h.size() * 4 + 4);
+  IRT_CUDA(cudaMemcpy(dst.p, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
+}
+}  // namespace
+
+Codec::Codec(int dev, const std::string& path, int precision) : device(dev), prec(precision) {
+  IRT_CUDA(cudaSetDevice(dev));
+  IRT_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  SafeTensorsFile st(path);
+  auto get = [&](const std::string& k, size_t rank) -> const TensorView& { return st.get(k, rank); };
+  auto conv = [&](Conv& c, const std::string& p, int dil) {
+    const TensorView& w = get(p + ".weight", 3);
+    c.cout = (int)w.shape[0];
+    c.cin = (int)w.shape[1];
+    c.k = (int)w.shape[2];
+    c.dil = dil;
+    c.pad = (c.k - 1) * dil / 2;  // conv_pad(k, 1, dil) (src/codec/layers.rs:64-66)
+    up_f32(c.w, w);
+    if (st.has(p + ".bias")) up_f32(c.b, get(p + ".bias", 1));
+  };
+  conv(qout, "quantizer.out_proj", 1);
+  conv(stem, "decoder.model.0", 1);
+  const int rates[4] = {12, 10, 8, 2};
+  for (int i = 0; i < 4; ++i) {
+    Block& bl = blocks[i];
+    std::string p = "decoder.model." + std::to_string(i + 1);
+    bl.stride = rates[i];
+    up_f32(bl.alpha, get(p + ".block.0.alpha", 3));
+    const TensorView& w = get(p + ".block.1.weight", 3);
+    bl.ct.cin = (int)w.shape[0];
+    bl.ct.cout = (int)w.shape[1];
+    bl.ct.k = (int)w.shape[2];
+    if (bl.ct.k != 2 * bl.stride) throw shape_error(p + ".block.1.weight kernel != 2*stride");
+    bl.ct.pad = (bl.stride + 1) / 2;  // conv_transpose_pad (src/codec/layers.rs:71-75)
+    up_f32(bl.ct.w, w);
+    if (st.has(p + ".block.1.bias")) up_f32(bl.ct.b, get(p + ".block.1.bias", 1));
+    const int ids[3] = {4, 5, 8}, dils[3] = {1, 3, 9};
+    for (int r = 0; r < 3; ++r) {
+      std::string q = p + ".block." + std::to_string(ids[r]);
+      up_f32(bl.res[r].a0, get(q + ".block.0.alpha", 3));
+      conv(bl.res[r].c1, q + ".block.1", dils[r]);
+      up_f32(bl.res[r].a2, get(q + ".block.2.alpha", 3));
+      conv(bl.res[r].c3, q + ".block.3", 1);
+    }
+  }
+  up_f32(head_alpha, get("decoder.wm_model.encoder_block.pre.0.alpha", 3));
+  conv(head, "decoder.wm_model.encoder_block.pre.1", 1);
+  if (qout.cin != 32) throw shape_error("quantizer.out_proj expects 32 latent channels");
+}
+
+Codec::~Codec() {
+  cudaSetDevice(device);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+void Codec::decode(const float* latent, int B, int T, float* wav, int memory, cudaStream_t user_stream) {
+  std::lock_guard<std::mutex> lock(mu);
+  IRT_CUDA(cudaSetDevice(device));
+  cudaStream_t s = user_stream ? user_stream : stream;
+  if (B <= 0 || T <= 0) throw shape_error("decode needs batch > 0 and frames > 0");
+  const long long l0 = launch_counter().load();
+  long maxel = (long)B * T * 32;
+  long t = T;
+  maxel = std::max(maxel, (long)B * stem.cout * t);
+  for (int i = 0; i < 4; ++i) {
+    t *= blocks[i].stride;
+    maxel = std::max(maxel, (long)B * blocks[i].ct.cout * t);
+  }
+  const long Tout = t;
+  for (auto* b : {&buf0, &buf1, &buf2}) b->ensure((size_t)maxel * 4 + 16);
+  in.ensure((size_t)B * T * 32 * 4 + 16);
+  IRT_CUDA(cudaMemcpyAsync(in.p, latent, (size_t)B * T * 32 * 4,
+                           memory == IRT_MEM_DEVICE ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
+  float* a = buf0.as<float>();
+  float* b = buf1.as<float>();
+  float* c = buf2.as<float>();
+  transpose_btc_bct(in.as<float>(), c, B, T, 32, s);  // [B,T,32] -> [B,32,T]
+  conv1d(c, B, 32, T, qout.w.as<float>(), qout.b.as<float>(), qout.cout, 1, 1, 0, nullptr, nullptr, 0, a, s);
+  conv1d(a, B, qout.cout, T, stem.w.as<float>(), stem.b.as<float>(), stem.cout, stem.k, 1, stem.pad, nullptr, nullptr,
+         0, b, s);
+  int C = stem.cout;
+  long cur = T;
+  std::swap(a, b);  // a = current activation
+  for (int i = 0; i < 4; ++i) {
+    Block& bl = blocks[i];
+    long nt = cur * bl.stride;
+    // Snake -> ConvTranspose (src/codec/decoder.rs:26-33)
+    conv_transpose1d(a, B, C, (int)cur, bl.ct.w.as<float>(), bl.ct.b.as<float>(), bl.ct.cout, bl.stride, bl.ct.pad,
+                     bl.alpha.as<float>(), b, (int)nt, s);
+    C = bl.ct.cout;
+    cur = nt;
+    std::swap(a, b);
+    for (int r = 0; r < 3; ++r) {
+      Res& ru = bl.res[r];
+      // Snake -> conv k7 dil -> Snake -> conv 1x1 -> + x  (src/codec/layers.rs:52-60)
+      conv1d(a, B, C, (int)cur, ru.c1.w.as<float>(), ru.c1.b.as<float>(), C, ru.c1.k, ru.c1.dil, ru.c1.pad,
+             ru.a0.as<float>(), nullptr, 0, b, s);
+      conv1d(b, B, C, (int)cur, ru.c3.w.as<float>(), ru.c3.b.as<float>(), C, 1, 1, 0, ru.a2.as<float>(), a, 0, c, s);
+      std::swap(a, c);
+    }
+  }
+  // head: Snake -> conv(96 -> 1, k7) -> tanh (src/codec/decoder.rs:43-54)
+  conv1d(a, B, C, (int)cur, head.w.as<float>(), head.b.as<float>(), 1, head.k, 1, head.pad, head_alpha.as<float>(),
+         nullptr, 1, b, s);
+  IRT_CUDA(cudaMemcpyAsync(wav, b, (size_t)B * Tout * 4,
+                           memory == IRT_MEM_DEVICE ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, s));
+  IRT_CUDA(cudaStreamSynchronize(s));
+  last_launches = launch_counter().load() - l0;
+}
+
+}  // namespace irt

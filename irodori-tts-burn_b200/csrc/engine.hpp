@@ -1,0 +1,94 @@
+// Engine: the loaded, pre-packed DiT + condition encoders on one device and
+// the rectified-flow sampler that drives them (src/inference.rs:83-254,
+// src/rf/euler_sampler.rs:132-718).
+#pragma once
+
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.hpp"
+#include "config.hpp"
+#include "kernels.hpp"
+
+namespace irt {
+
+class SafeTensorsFile;
+
+// TextBlock stack (src/model/text_encoder.rs:17-60) used by the text,
+// caption and speaker encoders.
+struct EncoderW {
+  int dim = 0, heads = 0, hd = 0, layers = 0, F = 0, Fp = 0, vocab = 0, in_dim = 0;
+  DevBuf emb;          // f32 [vocab, dim] (text / caption)
+  DevBuf in_w, in_b;   // T [dim, in_dim], f32 [dim] (speaker in_proj)
+  struct Layer {
+    DevBuf attn_norm, wqkvg, qn, kn, wo, mlp_norm, w13, w2;
+  };
+  std::vector<Layer> blk;
+  DevBuf out_norm;     // text_norm / speaker_norm / caption_norm
+};
+
+struct DitLayerW {
+  DevBuf wqkvg, qn, kn, wo, w13, w2;
+};
+
+struct Engine {
+  int device = 0;
+  int prec = IRT_PREC_BF16;
+  bool bf = true;  // GEMM operand storage is bf16
+  cudaStream_t stream = nullptr;
+  ModelConfig cfg;
+  bool has_params = false;
+  irt_sampler_params params{};
+  std::mutex mu;
+
+  // dimensions
+  int D = 0, L = 0, H = 0, hd = 0, P = 0, F = 0, Fp = 0, R = 0, Temb = 0;
+  int aux_kind = 0;  // 0 none, 1 speaker, 2 caption
+  int aux_dim = 0;
+
+  // weights
+  EncoderW text_enc, aux_enc;
+  DevBuf cm0, cm1, cm2;               // cond_module, f32
+  DevBuf in_w, in_b;                  // in_proj
+  DevBuf ada_down[3], ada_up[3], ada_upb[3];  // per kind (shift, scale, gate), stacked over (layer, attn|mlp)
+  std::vector<DitLayerW> blk;
+  DevBuf ctx_text_w, ctx_aux_w;       // [L*2D, td] / [L*2D, ad]: per layer [Wk; Wv]
+  DevBuf kn_all;                      // f32 [L, D]
+  DevBuf out_norm, out_w, out_b;
+
+  // workspaces (grow-only)
+  struct WS {
+    DevBuf x, h, q, k, v, g, attn, hm, xin, vout, raw, tokpos, seqs, vcomb, xpred, v1, hist[4], xstate, scal;
+    DevBuf ex, eh, eq, ek, ev, eg, eattn, ehm, estate, estate2, emask, eseq, etok;  // encoders
+    DevBuf cache_k, cache_v, rowmap_t, rowmap_a, rowmap_as, amask, aux_state_t;
+    DevBuf ada, temb, ce, su, dn;
+    DevBuf ids, tmask, ref, rmask, cids, cmask, noise, out;
+    DevBuf rope_cos, rope_sin;
+    DevBuf text_t, lat_t, st2, amask_in, amaskf, h0, h1, uo, ul, rows;
+  } ws;
+
+  long long last_row_forwards = 0, last_launches = 0;
+
+  Engine(int dev, const std::string& path, int precision);
+  ~Engine();
+
+  void sample(const irt_request& req, float* out, int out_memory, cudaStream_t user_stream);
+
+  // helpers
+  size_t esz() const { return bf ? 2 : 4; }
+  void gemm(const void* A, long lda, const DevBuf& W, int M, int N, int K, EpiParams p, cudaStream_t s);
+  void run_encoder(EncoderW& e, int B, int T, const void* input_rows_T, bool from_ids, const uint8_t* d_mask,
+                   const float* d_maskf, void* out_state_f32, cudaStream_t s);
+  void dit_forward(int M, const SeqDesc* d_seqs, int nseq, int max_len, int t_index, int nrows_ctx,
+                   cudaStream_t s);
+
+ private:
+  void load(const std::string& path);
+  void load_encoder(const SafeTensorsFile& st, EncoderW& e, const std::string& prefix, int dim, int heads,
+                    int layers, double ratio, bool embedding, int vocab, int in_dim);
+};
+
+}  // namespace irt

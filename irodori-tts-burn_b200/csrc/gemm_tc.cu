@@ -1,0 +1,407 @@
+// tcgen05 / TMEM / TMA bf16 GEMM for sm_100a with fused epilogues.
+//
+//   C[M,N] = A[M,K] . B[N,K]^T   (A activations, B PyTorch-layout weights;
+//                                 both K-major, bf16; fp32 accumulate in TMEM)
+//
+// Persistent, warp-specialised CTA of 192 threads:
+//   warp 0      TMA producer: A tile 128x64 and B tile BNx64 per stage (128B swizzle)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16)
+//   warps 2..5  epilogue: tcgen05.ld 32x32b -> registers -> fused epilogue -> global
+// Two TMEM accumulator buffers let the epilogue of tile i overlap the MMAs of
+// tile i+1.  Tiles are walked N-major (consecutive CTAs share a weight tile
+// through L2).  Every mbarrier wait is bounded by a 4 s watchdog that sets a
+// device error flag instead of hanging.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.hpp"
+#include "epilogue.cuh"
+
+namespace irt {
+
+__device__ int g_kernel_error = 0;
+
+int read_and_clear_kernel_error() {
+  int v = 0, z = 0;
+  cudaMemcpyFromSymbol(&v, g_kernel_error, sizeof(int));
+  if (v) cudaMemcpyToSymbol(g_kernel_error, &z, sizeof(int));
+  return v;
+}
+
+namespace tc {
+
+constexpr int BM = 128, BK = 64, STAGES = 4, THREADS = 192;
+constexpr uint32_t A_BYTES = BM * BK * 2;
+
+template <int BN>
+struct Cfg {
+  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
+  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  // instruction descriptor, kind::f16: D=f32 (bit4), A=B=bf16 (bits 7,10), K-major
+  // both, N>>3 at bits 17-22, M>>4 at bits 24-28.
+  static constexpr uint32_t IDESC =
+      (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: returns after the phase completes, or after ~4 s with the
+// device error flag set (the kernel then runs to completion with bad data
+// instead of hanging the GPU).
+__device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return;
+  uint64_t t0 = globaltimer();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 256; ++i)
+      if (mbar_try_wait(bar, parity)) return;
+    if (globaltimer() - t0 > 4000000000ull) {
+      atomicExch(&g_kernel_error, 1);
+      return;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
+// 1024 bytes (SBO), sm100 descriptor version 1.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32], int off) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr + off));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+template <int N>
+struct Regs {
+  uint32_t r[N];
+  __device__ __forceinline__ float operator()(int j) const { return __uint_as_float(r[j]); }
+};
+
+template <int BN>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
+                const __grid_constant__ EpiParams ep) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2]; then tmem base slot
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (K + BK - 1) / BK;
+
+  auto full = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty = [&](int s) { return smem_u32(&bars[STAGES + s]); };
+  auto tfull = [&](int b) { return smem_u32(&bars[2 * STAGES + b]); };
+  auto tempty = [&](int b) { return smem_u32(&bars[2 * STAGES + 2 + b]); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull(b), 1);
+      mbar_init(tempty(b), 4);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          mbar_wait(empty(s), ph ^ 1);
+          uint8_t* a_dst = tiles + s * C::STAGE_BYTES;
+          uint8_t* b_dst = a_dst + A_BYTES;
+          mbar_expect_tx(full(s), C::STAGE_BYTES);
+          tma_load_2d(smem_u32(a_dst), &tmA, full(s), kb * BK, m0);
+          tma_load_2d(smem_u32(b_dst), &tmB, full(s), kb * BK, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t it = 0, tl = 0;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tl) {
+        const int buf = tl & 1;
+        const uint32_t aph = (tl >> 1) & 1;
+        mbar_wait(tempty(buf), aph ^ 1);
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          mbar_wait(full(s), ph);
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(tiles + s * C::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            umma_f16(d_tmem, sdesc(a_addr + kk * 32), sdesc(b_addr + kk * 32), C::IDESC, (kb | kk) != 0);
+          }
+          umma_commit(empty(s));  // frees the smem stage when these MMAs complete
+        }
+        umma_commit(tfull(buf));  // accumulator ready
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2..5 ----------------
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    uint32_t tl = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tl) {
+      const int buf = tl & 1;
+      const uint32_t aph = (tl >> 1) & 1;
+      const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+      mbar_wait(tfull(buf), aph);
+      tc_fence_after();
+      const int row = m0 + quad * 32 + lane;
+      const bool row_ok = row < M;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * BN;
+      if (ep.mode == EPI_QKVG || ep.mode == EPI_CTXKV) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 128) {
+          if (n0 + c >= N) break;
+          Regs<128> R;
+          uint32_t(&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&R.r[0]);
+          uint32_t(&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&R.r[32]);
+          uint32_t(&r2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&R.r[64]);
+          uint32_t(&r3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&R.r[96]);
+          tmem_ld32(taddr, r0, c);
+          tmem_ld32(taddr, r1, c + 32);
+          tmem_ld32(taddr, r2, c + 64);
+          tmem_ld32(taddr, r3, c + 96);
+          tmem_wait_ld();
+          if (row_ok) epi_head<128>(ep, row, n0 + c, R);
+        }
+      } else if (ep.mode == EPI_SWIGLU) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64) {
+          if (n0 + c >= N) break;
+          Regs<64> R;
+          uint32_t(&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&R.r[0]);
+          uint32_t(&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&R.r[32]);
+          tmem_ld32(taddr, r0, c);
+          tmem_ld32(taddr, r1, c + 32);
+          tmem_wait_ld();
+          if (row_ok) epi_chunk_swiglu(ep, row, n0 + c, R);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          if (n0 + c >= N) break;
+          Regs<32> R;
+          tmem_ld32(taddr, R.r, c);
+          tmem_wait_ld();
+          if (row_ok) {
+            if (ep.mode == EPI_RESID) epi_chunk_resid<32>(ep, row, n0 + c, R);
+            else epi_chunk_store<32>(ep, row, n0 + c, R);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty(buf));
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: tensor maps (cached per buffer), launch.
+// ---------------------------------------------------------------------------
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn get_encode() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  });
+  if (!fn) throw Error(IRT_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+struct MapKey {
+  const void* p;
+  long rows, cols, ld;
+  int box_rows;
+  bool operator==(const MapKey& o) const {
+    return p == o.p && rows == o.rows && cols == o.cols && ld == o.ld && box_rows == o.box_rows;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<const void*>()(k.p) ^ (std::hash<long>()(k.rows) * 31) ^ (std::hash<long>()(k.cols) * 131) ^
+           (std::hash<long>()(k.ld) * 1313) ^ (size_t)k.box_rows;
+  }
+};
+
+const CUtensorMap& tensor_map(const void* p, long rows, long cols, long ld, int box_rows) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  MapKey key{p, rows, cols, ld, box_rows};
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  CUtensorMap m;
+  cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t gstride[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = get_encode()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(p), gdim, gstride, box, estride,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error(IRT_E_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  if (cache.size() > 4096) cache.clear();
+  return cache.emplace(key, m).first->second;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN>
+void launch(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int K, const EpiParams& p,
+            cudaStream_t s) {
+  using C = Cfg<BN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    IRT_CUDA(cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
+    attr_set = true;
+  }
+  const CUtensorMap& ta = tensor_map(A, M, K, lda, BM);
+  const CUtensorMap& tb = tensor_map(B, N, K, ldb, BN);
+  int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  int grid = tiles < num_sms() ? tiles : num_sms();
+  gemm_kernel<BN><<<grid, THREADS, C::SMEM, s>>>(ta, tb, M, N, K, p);
+  IRT_CHECK_LAUNCH();
+}
+
+}  // namespace tc
+
+bool gemm_tc_supported(const EpiParams& p, int K, long lda, long ldb, const void* A, const void* B) {
+  if (K < tc::BK || (K % 8) || (lda % 8) || (ldb % 8)) return false;
+  if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15)) return false;
+  if (p.M < tc::BM || p.N < 128) return false;
+  if ((p.mode == EPI_QKVG || p.mode == EPI_CTXKV) && (p.hd != 128 || (p.Dq % 128))) return false;
+  if (p.mode == EPI_SWIGLU && (p.N % 64)) return false;
+  return true;
+}
+
+void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int K, const EpiParams& p,
+             cudaStream_t s) {
+  // BN = 256 when it divides the per-head/segment structure, else 128.
+  bool use256 = N >= 256;
+  if ((p.mode == EPI_QKVG || p.mode == EPI_CTXKV) && (p.Dq % 256)) use256 = false;
+  if (use256) tc::launch<256>(A, lda, B, ldb, M, N, K, p, s);
+  else tc::launch<128>(A, lda, B, ldb, M, N, K, p, s);
+}
+
+}  // namespace irt

@@ -1,0 +1,303 @@
+// Bandwidth-bound row-wise and elementwise kernels of the sampling path.
+// Each row kernel reads its row once, reduces in registers + shared memory,
+// and writes its output once (coalesced, vectorised where aligned).
+#include "common.hpp"
+#include "epilogue.cuh"
+#include "kernels.hpp"
+
+namespace irt {
+
+namespace {
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x < NT / 32) t = red[threadIdx.x];
+  if (w == 0) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (l == 0) red[0] = t;
+  }
+  __syncthreads();
+  float r = red[0];
+  __syncthreads();
+  return r;
+}
+
+// mode 0: RmsNorm  y = x / rms * w         (src/model/norm.rs:25-39)
+// mode 1: adaLN    y = x / rms * (1+scale) + shift   (src/model/norm.rs:160-172)
+template <int NT, bool OBF>
+__global__ void __launch_bounds__(NT) rownorm_kernel(const float* __restrict__ x, const float* __restrict__ a,
+                                                     const float* __restrict__ b, void* __restrict__ y, int D,
+                                                     float eps, int mode) {
+  __shared__ float red[32];
+  const long row = blockIdx.x;
+  const float* xr = x + row * D;
+  float ss = 0.f;
+  const bool vec = (D % 4) == 0;
+  if (vec) {
+    for (int i = threadIdx.x * 4; i < D; i += NT * 4) {
+      float4 v = *reinterpret_cast<const float4*>(xr + i);
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+  } else {
+    for (int i = threadIdx.x; i < D; i += NT) ss += xr[i] * xr[i];
+  }
+  ss = block_sum<NT>(ss, red);
+  const float rms = sqrtf(ss / (float)D + eps);
+  auto f = [&](int i, float v) {
+    float t = v / rms;
+    if (mode == 0) return a ? t * a[i] : t;
+    return t * (b[i] + 1.f) + a[i];
+  };
+  if (vec) {
+    for (int i = threadIdx.x * 4; i < D; i += NT * 4) {
+      float4 v = *reinterpret_cast<const float4*>(xr + i);
+      float o0 = f(i, v.x), o1 = f(i + 1, v.y), o2 = f(i + 2, v.z), o3 = f(i + 3, v.w);
+      if (OBF) {
+        bf16* yr = reinterpret_cast<bf16*>(y) + row * D + i;
+        __nv_bfloat162 p0 = __floats2bfloat162_rn(o0, o1), p1 = __floats2bfloat162_rn(o2, o3);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&p0);
+        u.y = *reinterpret_cast<uint32_t*>(&p1);
+        *reinterpret_cast<uint2*>(yr) = u;
+      } else {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + row * D + i) = make_float4(o0, o1, o2, o3);
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < D; i += NT) {
+      float o = f(i, xr[i]);
+      if (OBF) reinterpret_cast<bf16*>(y)[row * D + i] = __float2bfloat16_rn(o);
+      else reinterpret_cast<float*>(y)[row * D + i] = o;
+    }
+  }
+}
+
+void rownorm(const float* x, const float* a, const float* b, void* y, int out_bf16, int M, int D, float eps, int mode,
+             cudaStream_t s) {
+  if (M <= 0) return;
+  if (out_bf16) rownorm_kernel<256, true><<<M, 256, 0, s>>>(x, a, b, y, D, eps, mode);
+  else rownorm_kernel<256, false><<<M, 256, 0, s>>>(x, a, b, y, D, eps, mode);
+  IRT_CHECK_LAUNCH();
+}
+
+__global__ void embed_kernel(const int* ids, const uint8_t* mask, const float* table, float* x, int M, int D,
+                             int vocab) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)M * D) return;
+  int m = (int)(i / D), d = (int)(i % D);
+  int id = ids[m];
+  id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
+  float mk = mask ? (mask[m] ? 1.f : 0.f) : 1.f;
+  x[i] = table[(long)id * D + d] * mk;
+}
+
+__global__ void gather_kernel(const float* in, const int* src, void* out, int out_bf16, int M, int D) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)M * D) return;
+  int m = (int)(i / D), d = (int)(i % D);
+  int r = src ? src[m] : m;
+  float v = in[(long)r * D + d];
+  if (out_bf16) reinterpret_cast<bf16*>(out)[i] = __float2bfloat16_rn(v);
+  else reinterpret_cast<float*>(out)[i] = v;
+}
+
+__global__ void mask_rows_kernel(float* x, const uint8_t* mask, int M, int D) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)M * D) return;
+  if (!mask[i / D]) x[i] = x[i] * 0.f;
+}
+
+__global__ void silu_copy_kernel(const float* in, long ld_in, float* out, long ld_out, int M, int D) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)M * D) return;
+  int m = (int)(i / D), d = (int)(i % D);
+  out[(long)m * ld_out + d] = silu_f(in[(long)m * ld_in + d]);
+}
+
+// One block per (batch, 256-wide column slice).
+__global__ void mean_token_kernel(const float* state, const uint8_t* mask, float* out, uint8_t* mask_out, int S,
+                                  int D) {
+  const int b = blockIdx.y;
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  float cnt = 0.f;
+  for (int s2 = 0; s2 < S; ++s2) cnt += mask[(long)b * S + s2] ? 1.f : 0.f;
+  if (d < D) {
+    float sum = 0.f;
+    for (int s2 = 0; s2 < S; ++s2) {
+      float mk = mask[(long)b * S + s2] ? 1.f : 0.f;
+      float v = state[((long)b * S + s2) * D + d];
+      sum += v * mk;
+      out[((long)b * (S + 1) + s2 + 1) * D + d] = v;
+    }
+    out[(long)b * (S + 1) * D + d] = sum / fmaxf(cnt, 1.f);
+  }
+  if (blockIdx.x == 0) {
+    for (int s2 = threadIdx.x; s2 < S + 1; s2 += blockDim.x)
+      mask_out[(long)b * (S + 1) + s2] = s2 == 0 ? (cnt > 0.f ? 1 : 0) : mask[(long)b * S + s2 - 1];
+  }
+}
+
+// v = v0 + sum_k (v0 - vk) * s_k   in the reference's accumulation order
+// (src/rf/euler_sampler.rs:421-433, :464-468, :506-510).
+__global__ void cfg_combine_kernel(const float* v, int ngroups, const float* scales, long ntok_p, float* out) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= ntok_p) return;
+  float v0 = v[i];
+  float acc = v0;
+  for (int k = 1; k < ngroups; ++k) acc = acc + (v0 - v[k * ntok_p + i]) * scales[k - 1];
+  out[i] = acc;
+}
+
+__global__ void axpy_kernel(float* y, const float* x, float a, long n) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = y[i] + x[i] * a;
+}
+
+struct LinArgs {
+  const float* x[4];
+  float c[4];
+};
+__global__ void lincomb_kernel(float* out, LinArgs a, int nx, long n) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float r = a.x[0][i] * a.c[0];
+  for (int k = 1; k < nx; ++k) r = r + a.x[k][i] * a.c[k];
+  out[i] = r;
+}
+
+// (v * omt + x) * ratio / omt - x / omt   (src/rf/math.rs:38-52)
+__global__ void trescale_kernel(float* v, const float* x, float omt, float ratio, long n) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float xv = x[i];
+  v[i] = (v[i] * omt + xv) * ratio / omt - xv / omt;
+}
+
+__global__ void scale_kernel(float* x, float a, long n) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) x[i] = x[i] * a;
+}
+
+__global__ void scale_rows_kernel(void* buf, int is_bf16, long row_len, const int* rows, int nrows, float a) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)nrows * row_len) return;
+  long r = rows[i / row_len];
+  long idx = r * row_len + i % row_len;
+  if (is_bf16) {
+    bf16* p = reinterpret_cast<bf16*>(buf);
+    p[idx] = __float2bfloat16_rn(__bfloat162float(p[idx]) * a);
+  } else {
+    float* p = reinterpret_cast<float*>(buf);
+    p[idx] = p[idx] * a;
+  }
+}
+
+// Counter-based Gaussian: splitmix64 hash of (seed, index) -> two uniforms ->
+// Box-Muller (cos branch).
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+__global__ void gauss_kernel(float* x, long n, uint64_t seed) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  uint64_t h = splitmix64(seed ^ splitmix64((uint64_t)i));
+  float u1 = ((h >> 40) + 1) * (1.0f / 16777217.0f);  // (0, 1]
+  float u2 = ((h >> 16) & 0xFFFFFF) * (1.0f / 16777216.0f);
+  x[i] = sqrtf(-2.f * logf(u1)) * cospif(2.f * u2);
+}
+
+inline unsigned nblk(long n, int t = 256) { return (unsigned)((n + t - 1) / t); }
+
+}  // namespace
+
+void adaln_modulate(const float* x, const float* shift, const float* scale, void* h, int out_bf16, int M, int D,
+                    float eps, cudaStream_t s) {
+  rownorm(x, shift, scale, h, out_bf16, M, D, eps, 1, s);
+}
+void rms_norm(const float* x, const float* w, void* y, int out_bf16, int M, int D, float eps, cudaStream_t s) {
+  rownorm(x, w, nullptr, y, out_bf16, M, D, eps, 0, s);
+}
+void embed_rows_v(const int* ids, const uint8_t* mask, const float* table, float* x, int M, int D, int vocab,
+                  cudaStream_t s) {
+  if ((long)M * D == 0) return;
+  embed_kernel<<<nblk((long)M * D), 256, 0, s>>>(ids, mask, table, x, M, D, vocab);
+  IRT_CHECK_LAUNCH();
+}
+void embed_rows(const int* ids, const uint8_t* mask, const float* table, float* x, int M, int D, cudaStream_t s) {
+  embed_rows_v(ids, mask, table, x, M, D, 1 << 30, s);
+}
+void gather_rows(const float* in, const int* src_row, void* out, int out_bf16, int M, int D, cudaStream_t s) {
+  if ((long)M * D == 0) return;
+  gather_kernel<<<nblk((long)M * D), 256, 0, s>>>(in, src_row, out, out_bf16, M, D);
+  IRT_CHECK_LAUNCH();
+}
+void mask_rows(float* x, const uint8_t* mask, int M, int D, cudaStream_t s) {
+  if ((long)M * D == 0) return;
+  mask_rows_kernel<<<nblk((long)M * D), 256, 0, s>>>(x, mask, M, D);
+  IRT_CHECK_LAUNCH();
+}
+void silu_copy(const float* in, long ld_in, float* out, long ld_out, int M, int D, cudaStream_t s) {
+  if ((long)M * D == 0) return;
+  silu_copy_kernel<<<nblk((long)M * D), 256, 0, s>>>(in, ld_in, out, ld_out, M, D);
+  IRT_CHECK_LAUNCH();
+}
+void prepend_mean_token(const float* state, const uint8_t* mask, float* out, uint8_t* mask_out, int B, int S, int D,
+                        cudaStream_t s) {
+  if (B == 0) return;
+  dim3 grid((D + 255) / 256, B);
+  mean_token_kernel<<<grid, 256, 0, s>>>(state, mask, out, mask_out, S, D);
+  IRT_CHECK_LAUNCH();
+}
+void cfg_combine(const float* v_packed, const int*, const float* scales, int ngroups, const int*, int ntok, int P,
+                 float* v_out, cudaStream_t s) {
+  long n = (long)ntok * P;
+  if (n == 0) return;
+  cfg_combine_kernel<<<nblk(n), 256, 0, s>>>(v_packed, ngroups, scales, n, v_out);
+  IRT_CHECK_LAUNCH();
+}
+void axpy(float* y, const float* x, float a, long n, cudaStream_t s) {
+  if (n == 0) return;
+  axpy_kernel<<<nblk(n), 256, 0, s>>>(y, x, a, n);
+  IRT_CHECK_LAUNCH();
+}
+void lincomb(float* out, const float* const* xs, const float* coefs, int nx, long n, cudaStream_t s) {
+  if (n == 0) return;
+  LinArgs a{};
+  for (int k = 0; k < nx && k < 4; ++k) { a.x[k] = xs[k]; a.c[k] = coefs[k]; }
+  lincomb_kernel<<<nblk(n), 256, 0, s>>>(out, a, nx, n);
+  IRT_CHECK_LAUNCH();
+}
+void temporal_rescale(float* v, const float* x, float omt, float ratio, long n, cudaStream_t s) {
+  if (n == 0) return;
+  trescale_kernel<<<nblk(n), 256, 0, s>>>(v, x, omt, ratio, n);
+  IRT_CHECK_LAUNCH();
+}
+void scale_buf(float* x, float a, long n, cudaStream_t s) {
+  if (n == 0) return;
+  scale_kernel<<<nblk(n), 256, 0, s>>>(x, a, n);
+  IRT_CHECK_LAUNCH();
+}
+void scale_rows_bf16_or_f32(void* buf, int is_bf16, long row_len, const int* rows, int nrows, float a,
+                            cudaStream_t s) {
+  long n = (long)nrows * row_len;
+  if (n == 0) return;
+  scale_rows_kernel<<<nblk(n), 256, 0, s>>>(buf, is_bf16, row_len, rows, nrows, a);
+  IRT_CHECK_LAUNCH();
+}
+void gaussian_fill(float* x, long n, uint64_t seed, cudaStream_t s) {
+  if (n == 0) return;
+  gauss_kernel<<<nblk(n), 256, 0, s>>>(x, n, seed);
+  IRT_CHECK_LAUNCH();
+}
+
+}  // namespace irt

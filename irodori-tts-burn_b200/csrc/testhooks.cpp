@@ -1,0 +1,115 @@
+// Kernel-level entry points for the GPU unit tests only.  Built into a
+// separate library (libirodori_b200_testhooks.so) so the product ABI in
+// include/irodori_b200.h stays exactly the reference-facing surface.
+#include <string>
+#include <vector>
+
+#include "common.hpp"
+#include "kernels.hpp"
+
+#define IRTT_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+thread_local std::string g_err;
+template <class F>
+int guard(F&& f) {
+  try {
+    f();
+    return 0;
+  } catch (const irt::Error& e) {
+    g_err = e.what();
+    return e.status;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return 22;
+  }
+}
+}  // namespace
+
+IRTT_API const char* irtt_last_error() { return g_err.c_str(); }
+
+// C[M,N] (f32) = A[M,K] . B[N,K]^T with bf16 operands; path 0 = tcgen05, 1 = SIMT.
+IRTT_API int irtt_gemm_store(const void* A, const void* B, int M, int N, int K, float* C, int path) {
+  return guard([&] {
+    irt::EpiParams p;
+    p.mode = irt::EPI_STORE;
+    p.M = M;
+    p.N = N;
+    p.out = C;
+    p.ldo = N;
+    if (path == 0) {
+      if (!irt::gemm_tc_supported(p, K, K, K, A, B)) throw irt::Error(4, "shape not supported by tcgen05 path");
+      irt::gemm_tc(reinterpret_cast<const irt::bf16*>(A), K, reinterpret_cast<const irt::bf16*>(B), K, M, N, K, p,
+                   nullptr);
+    } else {
+      irt::DevBuf raw((size_t)M * N * 4);
+      irt::gemm_simt(A, 1, K, 0, B, 1, K, 0, raw.as<float>(), N, 0, M, N, K, 1, nullptr);
+      irt::epilogue_apply(p, raw.as<float>(), N, 0, 1, nullptr);
+      IRT_CUDA(cudaDeviceSynchronize());
+    }
+    IRT_CUDA(cudaDeviceSynchronize());
+    if (irt::read_and_clear_kernel_error()) throw irt::Error(20, "pipeline watchdog fired");
+  });
+}
+
+// Fused-epilogue GEMM for the QKVG / SWIGLU / RESID modes with bf16 operands.
+IRTT_API int irtt_gemm_epi(int mode, const void* A, const void* B, int M, int N, int K, int path, void* o0, void* o1,
+                           void* o2, void* o3, const float* w0, const float* w1, const float* cos_t,
+                           const float* sin_t, const int* tok_pos, int H, int hd, int rope_heads, float* x,
+                           const float* gate, int F) {
+  return guard([&] {
+    irt::EpiParams p;
+    p.mode = mode;
+    p.M = M;
+    p.N = N;
+    p.out_bf16 = 1;
+    p.q = o0; p.k = o1; p.v = o2; p.g = o3;
+    p.qn_w = w0; p.kn_w = w1;
+    p.rope_cos = cos_t; p.rope_sin = sin_t;
+    p.tok_pos = tok_pos;
+    p.H = H; p.hd = hd; p.rope_heads = rope_heads; p.Dq = H * hd;
+    p.x = x;
+    p.gate = gate;
+    p.h = o0;
+    p.F = F;
+    if (path == 0) {
+      if (!irt::gemm_tc_supported(p, K, K, K, A, B)) throw irt::Error(4, "shape not supported by tcgen05 path");
+      irt::gemm_tc(reinterpret_cast<const irt::bf16*>(A), K, reinterpret_cast<const irt::bf16*>(B), K, M, N, K, p,
+                   nullptr);
+    } else {
+      irt::DevBuf raw((size_t)M * N * 4);
+      irt::gemm_simt(A, 1, K, 0, B, 1, K, 0, raw.as<float>(), N, 0, M, N, K, 1, nullptr);
+      irt::epilogue_apply(p, raw.as<float>(), N, 0, 1, nullptr);
+      IRT_CUDA(cudaDeviceSynchronize());
+    }
+    IRT_CUDA(cudaDeviceSynchronize());
+    if (irt::read_and_clear_kernel_error()) throw irt::Error(20, "pipeline watchdog fired");
+  });
+}
+
+// Attention over per-sequence [self | context] keys; seqs is a host array of
+// nseq x {tok_start, len, ctx_off, ctx_len}.
+IRTT_API int irtt_attention(const void* q, const void* k, const void* v, const void* g, const void* ck,
+                            const void* cv, const uint8_t* key_mask, const int* seqs_host, int nseq, int H, int hd,
+                            void* out, int bf16_io) {
+  return guard([&] {
+    std::vector<irt::SeqDesc> sd(nseq);
+    int mx = 0;
+    for (int i = 0; i < nseq; ++i) {
+      sd[i] = {seqs_host[4 * i], seqs_host[4 * i + 1], seqs_host[4 * i + 2], seqs_host[4 * i + 3]};
+      mx = std::max(mx, sd[i].len);
+    }
+    irt::DevBuf d(sizeof(irt::SeqDesc) * std::max(1, nseq));
+    IRT_CUDA(cudaMemcpy(d.p, sd.data(), sizeof(irt::SeqDesc) * nseq, cudaMemcpyHostToDevice));
+    irt::AttnParams p{};
+    p.q = q; p.k = k; p.v = v; p.gsig = g; p.ck = ck; p.cv = cv; p.key_mask = key_mask;
+    p.seqs = d.as<irt::SeqDesc>();
+    p.nseq = nseq; p.max_len = mx; p.H = H; p.hd = hd;
+    p.scale = 1.0f / sqrtf((float)hd);
+    p.out = out;
+    irt::attention(p, bf16_io, nullptr);
+    IRT_CUDA(cudaDeviceSynchronize());
+  });
+}
+
+IRTT_API long long irtt_launch_count() { return irt::launch_counter().load(); }

@@ -1,0 +1,214 @@
+"""Kernel-level GPU tests: each CUDA kernel against a plain PyTorch fp32
+reference of the same op (through the test-hook library, not the product ABI)."""
+
+import ctypes
+import math
+
+import pytest
+
+from conftest import PKG_DIR
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+_hooks = None
+
+
+def hooks():
+    global _hooks
+    if _hooks is None:
+        p = PKG_DIR / "libirodori_b200_testhooks.so"
+        if not p.exists():
+            pytest.fail(f"{p} missing: run __graft_entry__.build()")
+        L = ctypes.CDLL(str(p))
+        L.irtt_last_error.restype = ctypes.c_char_p
+        L.irtt_gemm_store.argtypes = [ctypes.c_void_p] * 2 + [ctypes.c_int] * 3 + [ctypes.c_void_p, ctypes.c_int]
+        L.irtt_gemm_epi.argtypes = ([ctypes.c_int] + [ctypes.c_void_p] * 2 + [ctypes.c_int] * 4 + [ctypes.c_void_p] * 9
+                                    + [ctypes.c_int] * 3 + [ctypes.c_void_p] * 2 + [ctypes.c_int])
+        L.irtt_attention.argtypes = [ctypes.c_void_p] * 8 + [ctypes.c_int] * 3 + [ctypes.c_void_p, ctypes.c_int]
+        _hooks = L
+    return _hooks
+
+
+def check(rc):
+    assert rc == 0, hooks().irtt_last_error().decode()
+
+
+def ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.fail("CUDA device required for -m gpu tests")
+    return torch.device("cuda:0")
+
+
+GEMM_SHAPES = [
+    (128, 256, 64),      # single tile
+    (300, 384, 736),     # M, N tails + K tail (736 = 11.5 x 64)
+    (1500, 2048, 2048),  # DiT Wo shape at the CFG batch
+    (1500, 8192, 2048),  # fused QKV+gate
+    (750, 128, 2048),    # out_proj (BN = 128 path)
+    (577, 2048, 5888),   # W2 with K = 5888
+]
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+@pytest.mark.parametrize("path", [0, 1])
+def test_gemm_store_matches_torch(dev, M, N, K, path):
+    if path == 1 and M * N * K > 2e9:
+        pytest.skip("SIMT path checked on the smaller shapes")
+    g = torch.Generator(device=dev).manual_seed(M * 7 + N * 3 + K)
+    A = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    B = torch.randn(N, K, device=dev, generator=g).to(torch.bfloat16)
+    C = torch.full((M, N), float("nan"), device=dev)
+    check(hooks().irtt_gemm_store(ptr(A), ptr(B), M, N, K, ptr(C), path))
+    ref = A.float() @ B.float().T
+    err = (C - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 2e-5, f"rel max err {err}"
+
+
+def _rope_tables(hd, S):
+    half = hd // 2
+    i = torch.arange(half, dtype=torch.float32)
+    fr = 1.0 / torch.pow(torch.tensor(10000.0), 2.0 * i / hd)
+    ang = torch.arange(S, dtype=torch.float32)[:, None] * fr[None]
+    return torch.cos(ang), torch.sin(ang)
+
+
+@pytest.mark.parametrize("path", [0, 1])
+def test_gemm_qkvg_epilogue(dev, path):
+    M, H, hd = 300, 4, 128
+    D = H * hd
+    g = torch.Generator(device=dev).manual_seed(11)
+    A = torch.randn(M, D, device=dev, generator=g).to(torch.bfloat16)
+    W = (torch.randn(4 * D, D, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    qn = 1 + 0.1 * torch.randn(D, device=dev, generator=g)
+    kn = 1 + 0.1 * torch.randn(D, device=dev, generator=g)
+    cos, sin = (t.to(dev).contiguous() for t in _rope_tables(hd, 200))
+    pos = (torch.arange(M, device=dev) % 150).to(torch.int32)
+    outs = [torch.zeros(M, D, device=dev, dtype=torch.bfloat16) for _ in range(4)]
+    check(hooks().irtt_gemm_epi(1, ptr(A), ptr(W), M, 4 * D, D, path, *[ptr(o) for o in outs], ptr(qn), ptr(kn),
+                                ptr(cos), ptr(sin), ptr(pos), H, hd, H // 2, None, None, 0))
+    acc = A.float() @ W.float().T
+    q, k, v, gg = acc.split(D, dim=1)
+
+    def norm_rope(x, w):
+        x = x.reshape(M, H, hd)
+        x = x / torch.sqrt((x * x).mean(-1, keepdim=True) + 1e-5) * w.reshape(H, hd)
+        c = cos[pos.long()][:, None, :]
+        s = sin[pos.long()][:, None, :]
+        re, im = x[..., 0::2], x[..., 1::2]
+        rot = torch.stack([re * c - im * s, re * s + im * c], dim=-1).reshape(M, H, hd)
+        x = torch.cat([rot[:, : H // 2], x[:, H // 2:]], dim=1)
+        return x.reshape(M, D)
+
+    refs = [norm_rope(q, qn), norm_rope(k, kn), v, torch.sigmoid(gg)]
+    for o, r, name in zip(outs, refs, "qkvg"):
+        err = (o.float() - r).abs().max().item() / r.abs().max().item()
+        assert err < 1e-2, f"{name}: rel err {err}"
+
+
+@pytest.mark.parametrize("path", [0, 1])
+def test_gemm_swiglu_and_resid(dev, path):
+    M, D, F = 257, 256, 736
+    Fp = (F + 31) // 32 * 32
+    g = torch.Generator(device=dev).manual_seed(5)
+    A = torch.randn(M, D, device=dev, generator=g).to(torch.bfloat16)
+    W1 = torch.randn(F, D, device=dev, generator=g) * 0.05
+    W3 = torch.randn(F, D, device=dev, generator=g) * 0.05
+    packed = torch.zeros(2 * Fp, D, device=dev)
+    for j in range(Fp // 32):
+        n = min(32, F - 32 * j)
+        packed[64 * j:64 * j + n] = W1[32 * j:32 * j + n]
+        packed[64 * j + 32:64 * j + 32 + n] = W3[32 * j:32 * j + n]
+    packed = packed.to(torch.bfloat16)
+    h = torch.zeros(M, F, device=dev, dtype=torch.bfloat16)
+    check(hooks().irtt_gemm_epi(3, ptr(A), ptr(packed), M, 2 * Fp, D, path, ptr(h), None, None, None, None, None,
+                                None, None, None, 0, 0, 0, None, None, F))
+    a = A.float() @ W1.to(torch.bfloat16).float().T
+    b = A.float() @ W3.to(torch.bfloat16).float().T
+    ref = torch.nn.functional.silu(a) * b
+    err = (h.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-2, f"swiglu rel err {err}"
+    # residual with gate: x = x + gate * (h @ W2^T)
+    W2 = (torch.randn(D, F, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    x = torch.randn(M, D, device=dev, generator=g)
+    gate = torch.randn(D, device=dev, generator=g)
+    x_ref = x + gate * (h.float() @ W2.float().T)
+    check(hooks().irtt_gemm_epi(2, ptr(h), ptr(W2), M, D, F, path, None, None, None, None, None, None, None, None,
+                                None, 0, 0, 0, ptr(x), ptr(gate), 0))
+    err = (x - x_ref).abs().max().item() / x_ref.abs().max().item()
+    assert err < 1e-4, f"resid rel err {err}"
+
+
+def _attn_ref(q, k, v, g, ck, cv, key_mask, seqs, H, hd):
+    out = torch.zeros_like(q, dtype=torch.float32)
+    for (ts, ln, co, cl) in seqs:
+        qs = q[ts:ts + ln].float().reshape(ln, H, hd)
+        ks = [k[ts:ts + ln].float().reshape(ln, H, hd)]
+        vs = [v[ts:ts + ln].float().reshape(ln, H, hd)]
+        valid = [torch.ones(ln, dtype=torch.bool, device=q.device) if key_mask is None
+                 else key_mask[ts:ts + ln].bool()]
+        if cl:
+            ks.append(ck[co:co + cl].float().reshape(cl, H, hd))
+            vs.append(cv[co:co + cl].float().reshape(cl, H, hd))
+            valid.append(torch.ones(cl, dtype=torch.bool, device=q.device))
+        K_, V_, m = torch.cat(ks), torch.cat(vs), torch.cat(valid)
+        s = torch.einsum("qhd,khd->hqk", qs, K_) / math.sqrt(hd)
+        s = s.masked_fill(~m[None, None], float("-inf"))
+        w = torch.nan_to_num(torch.softmax(s, -1), nan=0.0)
+        o = torch.einsum("hqk,khd->qhd", w, V_).reshape(ln, H * hd)
+        out[ts:ts + ln] = o * (g[ts:ts + ln].float() if g is not None else 1)
+    return out
+
+
+@pytest.mark.parametrize("bf16", [1, 0])
+def test_attention_matches_torch(dev, bf16):
+    H, hd = 4, 128
+    D = H * hd
+    seqs = [(0, 150, 0, 77), (150, 64, 77, 0), (214, 1, 77, 5), (215, 90, 82, 130)]
+    M = 305
+    nctx = 212
+    dt = torch.bfloat16 if bf16 else torch.float32
+    g = torch.Generator(device=dev).manual_seed(3)
+    mk = lambda n: torch.randn(n, D, device=dev, generator=g).to(dt)
+    q, k, v, ck, cv = mk(M), mk(M), mk(M), mk(nctx), mk(nctx)
+    gs = torch.sigmoid(torch.randn(M, D, device=dev, generator=g)).to(dt)
+    out = torch.zeros(M, D, device=dev, dtype=dt)
+    sd = (ctypes.c_int * 16)(*[x for s in seqs for x in s])
+    check(hooks().irtt_attention(ptr(q), ptr(k), ptr(v), ptr(gs), ptr(ck), ptr(cv), None, sd, len(seqs), H, hd,
+                                 ptr(out), bf16))
+    ref = _attn_ref(q, k, v, gs, ck, cv, None, seqs, H, hd)
+    err = (out.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < (2e-2 if bf16 else 1e-5), f"attention rel err {err}"
+
+
+@pytest.mark.parametrize("bf16", [1, 0])
+def test_attention_key_mask_and_empty_rows(dev, bf16):
+    """Masked self keys are skipped; a sequence whose keys are all masked
+    yields exactly 0 (safe softmax), even with NaN in the masked V rows."""
+    H, hd = 2, 128
+    D = H * hd
+    M = 96
+    dt = torch.bfloat16 if bf16 else torch.float32
+    g = torch.Generator(device=dev).manual_seed(9)
+    q = torch.randn(M, D, device=dev, generator=g).to(dt)
+    k = torch.randn(M, D, device=dev, generator=g).to(dt)
+    v = torch.randn(M, D, device=dev, generator=g).to(dt)
+    mask = torch.ones(M, dtype=torch.uint8, device=dev)
+    mask[40:64] = 0          # tail padding of sequence 0
+    mask[64:96] = 0          # sequence 1 entirely masked
+    v[64:96] = float("nan")  # masked keys must not leak NaN
+    v[40:64] = float("nan")
+    seqs = [(0, 64, 0, 0), (64, 32, 0, 0)]
+    out = torch.full((M, D), 7.0, device=dev, dtype=dt)
+    sd = (ctypes.c_int * 8)(*[x for s in seqs for x in s])
+    check(hooks().irtt_attention(ptr(q), ptr(k), ptr(v), None, None, None, ptr(mask), sd, 2, H, hd, ptr(out), bf16))
+    assert torch.isfinite(out.float()).all()
+    assert (out[64:96].float() == 0).all()
+    ref = _attn_ref(q, k, torch.nan_to_num(v), None, None, None, mask, seqs[:1], H, hd)
+    err = (out[:64].float() - ref[:64]).abs().max().item() / ref[:64].abs().max().item()
+    assert err < (2e-2 if bf16 else 1e-5), f"rel err {err}"
