@@ -444,10 +444,14 @@ class InferenceEngine:
             raise IrodoriError(22, "request arrays must be all on the host or all on the GPU")
         r.memory = MEM_DEVICE if all(devs) else MEM_HOST
         r.seed = int(request.seed)
+        import numpy as np
         if out is None:
-            import numpy as np
-            res = np.empty((B, S, P), dtype=np.float32)
-            o_p, o_mem = res.ctypes.data, MEM_HOST
+            out = np.empty((B, S, P), dtype=np.float32)
+        if isinstance(out, np.ndarray):
+            if out.shape != (B, S, P) or out.dtype != np.float32 or not out.flags["C_CONTIGUOUS"]:
+                raise IrodoriError(2, "Shape mismatch: out must be a contiguous float32 [B, S, P] array")
+            res = out
+            o_p, o_mem = out.ctypes.data, MEM_HOST
         else:
             if tuple(out.shape) != (B, S, P) or not out.is_contiguous():
                 raise IrodoriError(2, "Shape mismatch: out must be a contiguous [B, S, P] tensor")

@@ -626,8 +626,10 @@ def joint_attention(W: Weights, p: str, h: Tensor, kv: KvCache, cos, sin, latent
     cfg = W.cfg
     B, S, D = h.shape
     H, hd, eps = cfg.num_heads, cfg.head_dim(), cfg.norm_eps
-    wqkv = torch.cat([W[f"{p}.wq.weight"], W[f"{p}.wk.weight"], W[f"{p}.wv.weight"]], 0)
-    qkv = h @ wqkv.T
+    key = f"{p}.__fused_qkv"  # prepare_for_inference (src/model/attention.rs:514-523), built once
+    if key not in W.t:
+        W.t[key] = torch.cat([W[f"{p}.wq.weight"], W[f"{p}.wk.weight"], W[f"{p}.wv.weight"]], 0)
+    qkv = h @ W.t[key].T
     q, k, v = (qkv[..., i * D:(i + 1) * D].reshape(B, S, H, hd) for i in range(3))
     q = apply_rotary_half(head_rms_norm(q, W[f"{p}.q_norm.weight"], eps), cos, sin)
     k = apply_rotary_half(head_rms_norm(k, W[f"{p}.k_norm.weight"], eps), cos, sin)
@@ -656,8 +658,10 @@ def dit_forward(W: Weights, x_t: Tensor, t: Tensor, kv: List[KvCache], cos, sin,
         h, g = low_rank_adaln(W, f"{b}.attention_adaln", x, ce, eps)
         x = x + g * joint_attention(W, f"{b}.attention", h, kv[i], cos, sin, latent_mask)
         h, g = low_rank_adaln(W, f"{b}.mlp_adaln", x, ce, eps)
-        w13 = torch.cat([W[f"{b}.mlp.w1.weight"], W[f"{b}.mlp.w3.weight"]], 0)
-        a = h @ w13.T
+        key = f"{b}.mlp.__fused_w13"  # src/model/feed_forward.rs:96-103, built once
+        if key not in W.t:
+            W.t[key] = torch.cat([W[f"{b}.mlp.w1.weight"], W[f"{b}.mlp.w3.weight"]], 0)
+        a = h @ W.t[key].T
         F_ = a.shape[-1] // 2
         x = x + g * ((silu(a[..., :F_]) * a[..., F_:]) @ W[f"{b}.mlp.w2.weight"].T)
         if capture:
