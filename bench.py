@@ -353,9 +353,22 @@ def main():
     ap.add_argument("--skip-latency", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--ckpt", default=None)
+    ap.add_argument("--latency-only", action="store_true",
+                    help="only the config-3 single-utterance latency (used for profiling runs)")
+    ap.add_argument("--gemm-case", type=int, default=0,
+                    help="only the four DiT GEMMs of one layer at M rows, --steps times (profiling case)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.latency_only:
+        return latency_only(args)
+    if args.gemm_case:
+        import torch
+        load_pkg()
+        achieved, ms, flops = gemm_roofline(args.gemm_case, reps=args.steps)
+        print(json.dumps({"gemm_case_M": args.gemm_case, "achieved_tflops": round(achieved, 1),
+                          "ms_per_layer": round(ms, 4), "gflop_per_layer": round(flops / 1e9, 2)}), flush=True)
+        return 0
 
     import torch
     rank = int(os.environ.get("RANK", "0"))
@@ -473,6 +486,39 @@ def main():
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+    return 0
+
+
+def latency_only(args):
+    """Config-3 latency alone: one checkpoint load, `--warmup` untimed and
+    `--steps` timed sample() calls for the default CFG window."""
+    import torch
+    pkg = load_pkg()
+    cfg = model_cfg()
+    ckpt = Path(args.ckpt) if args.ckpt else Path(tempfile.gettempdir()) / "irodori_bench" / "dit_default_l32_s4.safetensors"
+    ensure_checkpoint(ckpt, cfg, 0, 1)
+    params = pkg.SamplerParams(num_steps=40, guidance=pkg.GuidanceConfig(mode="joint", scale_text=3.0,
+                                                                         scale_speaker=3.0))
+    eng = pkg.InferenceBuilder(0).load_weights(str(ckpt), precision="bf16").with_sampling(params).build()
+    import irodori_b200.synth as synth
+    r = synth.make_request(cfg, 1, 200, 375, 750, seed=3)
+    d = {k: v.cuda() for k, v in r.items() if torch.is_tensor(v)}
+    out = torch.empty(1, 750, cfg["latent_dim"], device="cuda")
+    rq = pkg.SamplingRequest(sequence_length=750, **d)
+    st = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        eng.sample(rq, out=out, stream=st)
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        eng.sample(rq, out=out, stream=st)
+        e1.record(st)
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    rows, launches = eng.last_stats()
+    print(json.dumps({"latency_ms": ts, "row_forwards": rows, "kernel_launches": launches}), flush=True)
     return 0
 
 

@@ -8,9 +8,9 @@
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16)
 //   warps 2..5  epilogue: tcgen05.ld 32x32b -> registers -> fused epilogue -> global
 // Two TMEM accumulator buffers let the epilogue of tile i overlap the MMAs of
-// tile i+1.  Tiles are walked N-major (consecutive CTAs share a weight tile
-// through L2).  Every mbarrier wait is bounded by a 4 s watchdog that sets a
-// device error flag instead of hanging.
+// tile i+1.  Tiles are walked in grouped order (see tile_coords).  Every
+// mbarrier wait is bounded by a 4 s watchdog that sets a device error flag
+// instead of hanging.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -137,6 +137,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32], int
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Grouped rasterisation: tiles are walked in groups of GROUP_M m-tiles; inside
+// a group n is the outer and m the inner index.  Concurrent CTAs then share a
+// few weight tiles and one group of activation rows (GROUP_M * 128 rows stay
+// L2-resident while every n-tile passes over them), so each operand comes
+// from HBM about once instead of once per n-tile.
+constexpr int GROUP_M = 16;
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& m_idx, int& n_idx) {
+  const int per_group = GROUP_M * n_tiles;
+  const int g = t / per_group;
+  const int r = t - g * per_group;
+  const int first_m = g * GROUP_M;
+  const int gm = min(GROUP_M, m_tiles - first_m);
+  n_idx = r / gm;
+  m_idx = first_m + (r - n_idx * gm);
+}
+
 template <int N>
 struct Regs {
   uint32_t r[N];
@@ -193,7 +209,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       uint32_t it = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-        const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+        int mi_, ni_;
+        tile_coords(t, m_tiles, n_tiles, mi_, ni_);
+        const int m0 = mi_ * BM, n0 = ni_ * BN;
         for (int kb = 0; kb < k_blocks; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -239,7 +257,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tl) {
       const int buf = tl & 1;
       const uint32_t aph = (tl >> 1) & 1;
-      const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+      int mi_, ni_;
+      tile_coords(t, m_tiles, n_tiles, mi_, ni_);
+      const int m0 = mi_ * BM, n0 = ni_ * BN;
       mbar_wait(tfull(buf), aph);
       tc_fence_after();
       const int row = m0 + quad * 32 + lane;

@@ -47,8 +47,6 @@ IRTT_API int irtt_gemm_store(const void* A, const void* B, int M, int N, int K, 
       irt::epilogue_apply(p, raw.as<float>(), N, 0, 1, nullptr);
       IRT_CUDA(cudaDeviceSynchronize());
     }
-    IRT_CUDA(cudaDeviceSynchronize());
-    if (irt::read_and_clear_kernel_error()) throw irt::Error(20, "pipeline watchdog fired");
   });
 }
 
@@ -82,8 +80,6 @@ IRTT_API int irtt_gemm_epi(int mode, const void* A, const void* B, int M, int N,
       irt::epilogue_apply(p, raw.as<float>(), N, 0, 1, nullptr);
       IRT_CUDA(cudaDeviceSynchronize());
     }
-    IRT_CUDA(cudaDeviceSynchronize());
-    if (irt::read_and_clear_kernel_error()) throw irt::Error(20, "pipeline watchdog fired");
   });
 }
 
@@ -113,3 +109,11 @@ IRTT_API int irtt_attention(const void* q, const void* k, const void* v, const v
 }
 
 IRTT_API long long irtt_launch_count() { return irt::launch_counter().load(); }
+
+// Synchronise the device and report the GEMM pipeline watchdog flag.
+IRTT_API int irtt_sync_check() {
+  return guard([&] {
+    IRT_CUDA(cudaDeviceSynchronize());
+    if (irt::read_and_clear_kernel_error()) throw irt::Error(20, "pipeline watchdog fired");
+  });
+}

@@ -32,6 +32,8 @@ def hooks():
 
 def check(rc):
     assert rc == 0, hooks().irtt_last_error().decode()
+    rc = hooks().irtt_sync_check()  # kernels are asynchronous; sync + watchdog flag
+    assert rc == 0, hooks().irtt_last_error().decode()
 
 
 def ptr(t):
