@@ -205,30 +205,43 @@ def gemm_roofline(M, reps=5):
     pos = (torch.arange(M, device=dev) % 1024).to(torch.int32)
     P = lambda t: ctypes.c_void_p(t.data_ptr())
 
-    def run():
-        rc = 0
-        rc |= L.irtt_gemm_epi(1, P(h), P(wqkvg), M, 4 * D, D, 0, *[P(o) for o in outs], P(nw), P(nw), P(cos), P(sin),
-                              P(pos), H, hd, H // 2, None, None, 0)
-        rc |= L.irtt_gemm_epi(2, P(outs[0]), P(wo), M, D, D, 0, None, None, None, None, None, None, None, None, None,
-                              0, 0, 0, P(x), P(gate), 0)
-        rc |= L.irtt_gemm_epi(3, P(h), P(w13), M, 2 * F, D, 0, P(hout), None, None, None, None, None, None, None,
-                              None, 0, 0, 0, None, None, F)
-        rc |= L.irtt_gemm_epi(2, P(hm), P(w2), M, D, F, 0, None, None, None, None, None, None, None, None, None, 0, 0,
-                              0, P(x), P(gate), 0)
+    def ck(rc):
         if rc:
             raise RuntimeError(L.irtt_last_error().decode())
+
+    parts = [
+        lambda: ck(L.irtt_gemm_epi(1, P(h), P(wqkvg), M, 4 * D, D, 0, *[P(o) for o in outs], P(nw), P(nw), P(cos),
+                                   P(sin), P(pos), H, hd, H // 2, None, None, 0)),
+        lambda: ck(L.irtt_gemm_epi(2, P(outs[0]), P(wo), M, D, D, 0, None, None, None, None, None, None, None, None,
+                                   None, 0, 0, 0, P(x), P(gate), 0)),
+        lambda: ck(L.irtt_gemm_epi(3, P(h), P(w13), M, 2 * F, D, 0, P(hout), None, None, None, None, None, None, None,
+                                   None, 0, 0, 0, None, None, F)),
+        lambda: ck(L.irtt_gemm_epi(2, P(hm), P(w2), M, D, F, 0, None, None, None, None, None, None, None, None, None,
+                                   0, 0, 0, P(x), P(gate), 0)),
+    ]
+
+    def run():
+        for fn in parts:
+            fn()
+
+    run.parts = parts
 
     run()
     torch.cuda.synchronize()
     st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    per = [0.0] * 4
     for _ in range(reps):
-        run()
-    e1.record(st)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / reps
+        ev[0].record(st)
+        for i, fn in enumerate(run.parts):
+            fn()
+            ev[i + 1].record(st)
+        torch.cuda.synchronize()
+        for i in range(4):
+            per[i] += ev[i].elapsed_time(ev[i + 1]) / reps
+    ms = sum(per)
     flops = 2.0 * M * D * (4 * D + D + 2 * F) + 2.0 * M * F * D
+    gemm_roofline.last_parts = {n: round(t, 4) for n, t in zip(("qkvg_ms", "wo_ms", "w13_ms", "w2_ms"), per)}
     return flops / (ms * 1e-3) / 1e12, ms, flops
 
 
@@ -367,7 +380,8 @@ def main():
         load_pkg()
         achieved, ms, flops = gemm_roofline(args.gemm_case, reps=args.steps)
         print(json.dumps({"gemm_case_M": args.gemm_case, "achieved_tflops": round(achieved, 1),
-                          "ms_per_layer": round(ms, 4), "gflop_per_layer": round(flops / 1e9, 2)}), flush=True)
+                          "ms_per_layer": round(ms, 4), "gflop_per_layer": round(flops / 1e9, 2),
+                          **gemm_roofline.last_parts}), flush=True)
         return 0
 
     import torch

@@ -95,6 +95,7 @@ void rope_tables_host(int hd, int S, std::vector<float>& cs, std::vector<float>&
 Engine::Engine(int dev, const std::string& path, int precision) : device(dev), prec(precision) {
   if (precision != IRT_PREC_BF16 && precision != IRT_PREC_F32) throw Error(IRT_E_INVALID_ARG, "invalid precision");
   bf = precision == IRT_PREC_BF16;
+  use_graphs = std::getenv("IRT_NO_GRAPHS") == nullptr;
   IRT_CUDA(cudaSetDevice(dev));
   IRT_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   load(path);
@@ -102,6 +103,7 @@ Engine::Engine(int dev, const std::string& path, int precision) : device(dev), p
 
 Engine::~Engine() {
   cudaSetDevice(device);
+  for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
   if (stream) cudaStreamDestroy(stream);
 }
 
@@ -424,7 +426,57 @@ void Engine::run_encoder(EncoderW& e, int B, int T, const void* input, bool from
 // One DiT forward over M packed rows (src/model/dit/model.rs:354-393):
 // input ws.xin [M, P] (operand type), output ws.vout [M, P] f32.
 // ---------------------------------------------------------------------------
-void Engine::dit_forward(int M, const SeqDesc* d_seqs, int nseq, int max_len, int t_index, int nrows_ctx,
+void Engine::forward_step(int M, const SeqDesc* d_seqs, int nseq, int max_len, int t_index, int nrows_ctx,
+                          cudaStream_t s) {
+  const size_t ada_bytes = (size_t)L * 6 * D * 4;
+  ada_cur.ensure(ada_bytes);
+  IRT_CUDA(cudaMemcpyAsync(ada_cur.p, ws.ada.as<uint8_t>() + (size_t)t_index * ada_bytes, ada_bytes,
+                           cudaMemcpyDeviceToDevice, s));
+  if (!use_graphs) {
+    dit_forward(M, d_seqs, nseq, max_len, ada_cur.as<float>(), nrows_ctx, s);
+    return;
+  }
+  std::vector<uintptr_t> key = {
+      (uintptr_t)M, (uintptr_t)d_seqs, (uintptr_t)nseq, (uintptr_t)max_len, (uintptr_t)nrows_ctx, (uintptr_t)s,
+      (uintptr_t)ws.x.p, (uintptr_t)ws.h.p, (uintptr_t)ws.q.p, (uintptr_t)ws.k.p, (uintptr_t)ws.v.p,
+      (uintptr_t)ws.g.p, (uintptr_t)ws.attn.p, (uintptr_t)ws.hm.p, (uintptr_t)ws.xin.p, (uintptr_t)ws.vout.p,
+      (uintptr_t)ws.raw.p, (uintptr_t)ws.tokpos.p, (uintptr_t)ws.cache_k.p, (uintptr_t)ws.cache_v.p,
+      (uintptr_t)ws.rope_cos.p, (uintptr_t)ws.rope_sin.p, (uintptr_t)ada_cur.p};
+  auto it = graphs.find(key);
+  if (it == graphs.end()) {
+    if (graph_seen[key]++ == 0) {  // first use: eager (allocations happen here)
+      dit_forward(M, d_seqs, nseq, max_len, ada_cur.as<float>(), nrows_ctx, s);
+      return;
+    }
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    const long long before = launch_counter().load();
+    IRT_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    try {
+      dit_forward(M, d_seqs, nseq, max_len, ada_cur.as<float>(), nrows_ctx, s);
+    } catch (...) {
+      cudaStreamEndCapture(s, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    IRT_CUDA(cudaStreamEndCapture(s, &g));
+    cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    IRT_CUDA(e);
+    if (graphs.size() > 64) {  // bound the cache
+      for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+      graphs.clear();
+    }
+    it = graphs.emplace(key, ge).first;
+    // kernels recorded in the graph (captured launches are not executed)
+    graph_kernels[key] = launch_counter().load() - before;
+    launch_counter().fetch_sub(graph_kernels[key]);
+  }
+  IRT_CUDA(cudaGraphLaunch(it->second, s));
+  launch_counter().fetch_add(graph_kernels[key]);
+}
+
+void Engine::dit_forward(int M, const SeqDesc* d_seqs, int nseq, int max_len, const float* ada_t, int nrows_ctx,
                          cudaStream_t s) {
   const float eps = (float)cfg.norm_eps;
   float* x = ws.x.as<float>();
@@ -436,7 +488,6 @@ void Engine::dit_forward(int M, const SeqDesc* d_seqs, int nseq, int max_len, in
     p.bias = in_b.as<float>();
     gemm(ws.xin.p, P, in_w, M, D, P, p, s);
   }
-  const float* ada_t = ws.ada.as<float>() + (size_t)t_index * L * 6 * D;
   for (int l = 0; l < L; ++l) {
     const float* ad = ada_t + (size_t)l * 6 * D;
     auto& b = blk[l];
@@ -479,13 +530,8 @@ void Engine::dit_forward(int M, const SeqDesc* d_seqs, int nseq, int max_len, in
     r2.gate = ad + 5 * D;
     gemm(ws.hm.p, F, b.w2, M, D, F, r2, s);
   }
-  rms_norm(x, out_norm.as<float>(), ws.h.p, bf, M, D, eps, s);
-  EpiParams o;
-  o.mode = EPI_STORE;
-  o.out = ws.vout.p;
-  o.ldo = P;
-  o.bias = out_b.as<float>();
-  gemm(ws.h.p, D, out_w, M, P, D, o, s);
+  // out_norm + out_proj fused (narrow N = P): one pass over x per row
+  rmsnorm_proj(x, out_norm.as<float>(), out_w.p, bf, out_b.as<float>(), ws.vout.as<float>(), M, D, P, eps, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -950,7 +996,7 @@ void Engine::sample(const irt_request& rq, float* out, int out_memory, cudaStrea
     // replicate x into each group's rows
     for (int g = 0; g < G; ++g)
       gather_rows(xin_f32, nullptr, ws.xin.as<uint8_t>() + (size_t)g * ntok * P * esz(), bf, ntok, P, s);
-    dit_forward(G * ntok, ws.seqs.as<SeqDesc>() + toff, G * B, Smax, t_index, nctx, s);
+    forward_step(G * ntok, ws.seqs.as<SeqDesc>() + toff, G * B, Smax, t_index, nctx, s);
     last_row_forwards += (long long)G * B;
     if (G == 1) {
       IRT_CUDA(cudaMemcpyAsync(v_out, ws.vout.p, nel * 4, cudaMemcpyDeviceToDevice, s));

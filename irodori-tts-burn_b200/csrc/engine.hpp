@@ -72,6 +72,17 @@ struct Engine {
 
   long long last_row_forwards = 0, last_launches = 0;
 
+  // CUDA graphs of the DiT forward, keyed by its shape and every buffer
+  // address it bakes in.  A key's first use runs eagerly (so workspaces are
+  // allocated outside capture); its second use captures and instantiates.
+  bool use_graphs = true;
+  std::map<std::vector<uintptr_t>, cudaGraphExec_t> graphs;
+  std::map<std::vector<uintptr_t>, int> graph_seen;
+  std::map<std::vector<uintptr_t>, long long> graph_kernels;
+  DevBuf ada_cur;  // adaLN parameters of the current step, read by the graph
+  void forward_step(int M, const SeqDesc* d_seqs, int nseq, int max_len, int t_index, int nrows_ctx,
+                    cudaStream_t s);
+
   Engine(int dev, const std::string& path, int precision);
   ~Engine();
 
@@ -82,7 +93,7 @@ struct Engine {
   void gemm(const void* A, long lda, const DevBuf& W, int M, int N, int K, EpiParams p, cudaStream_t s);
   void run_encoder(EncoderW& e, int B, int T, const void* input_rows_T, bool from_ids, const uint8_t* d_mask,
                    const float* d_maskf, void* out_state_f32, cudaStream_t s);
-  void dit_forward(int M, const SeqDesc* d_seqs, int nseq, int max_len, int t_index, int nrows_ctx,
+  void dit_forward(int M, const SeqDesc* d_seqs, int nseq, int max_len, const float* ada_t, int nrows_ctx,
                    cudaStream_t s);
 
  private:

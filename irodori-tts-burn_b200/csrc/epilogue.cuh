@@ -111,14 +111,34 @@ __device__ __forceinline__ void epi_chunk_resid(const EpiParams& p, int m, int n
   }
 }
 
+// Split-K partial of the gated residual: x += gate * acc with vector atomics
+// (the residual update is additive, so K-splits accumulate in any order).
+template <int W, class Acc>
+__device__ __forceinline__ void epi_chunk_resid_atomic(const EpiParams& p, int m, int n0, const Acc& acc) {
+  float* x = p.x + (long)m * p.N + n0;
+  if (n0 + W <= p.N && ((reinterpret_cast<uintptr_t>(x) & 15) == 0)) {
+#pragma unroll
+    for (int j = 0; j < W; j += 4) {
+      const float4 g = p.gate ? *reinterpret_cast<const float4*>(p.gate + n0 + j) : make_float4(1.f, 1.f, 1.f, 1.f);
+      atomicAdd(reinterpret_cast<float4*>(x + j),
+                make_float4(g.x * acc(j), g.y * acc(j + 1), g.z * acc(j + 2), g.w * acc(j + 3)));
+    }
+  } else {
+    for (int j = 0; j < W && n0 + j < p.N; ++j) atomicAdd(x + j, (p.gate ? p.gate[n0 + j] : 1.f) * acc(j));
+  }
+}
+
 // ---- SWIGLU: columns [n0, n0+32) = w1 group, [n0+32, n0+64) = w3 group -----
-template <class Acc>
+template <class Acc, bool FAST = false>
 __device__ __forceinline__ void epi_chunk_swiglu(const EpiParams& p, int m, int n0, const Acc& acc) {
   constexpr int G = SWIGLU_GROUP;
   int f0 = (n0 / (2 * G)) * G;
   float v[G];
 #pragma unroll
-  for (int j = 0; j < G; ++j) v[j] = silu_f(acc(j)) * acc(G + j);
+  for (int j = 0; j < G; ++j) {
+    const float a = acc(j);
+    v[j] = (FAST ? __fdividef(a, 1.f + __expf(-a)) : silu_f(a)) * acc(G + j);
+  }
   long base = (long)m * p.F + f0;
   if (f0 + G <= p.F) store_run<G>(p.h, base, p.out_bf16, v);
   else
@@ -171,6 +191,40 @@ __device__ __forceinline__ void epi_head(const EpiParams& p, int m, int n0, cons
   }
   const float* cs = rope ? p.rope_cos + (long)pos * (hd / 2) : nullptr;
   const float* sn = rope ? p.rope_sin + (long)pos * (hd / 2) : nullptr;
+  if constexpr (HD > 0) {
+    // Tensor-core path (bf16 outputs): reciprocal multiply, vectorised
+    // weight / table loads, fast sigmoid.
+    const float inv = 1.f / rms;
+#pragma unroll
+    for (int j0 = 0; j0 < HD; j0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = acc(j0 + j);
+      if (nw) {
+        const float4 w0 = *reinterpret_cast<const float4*>(nw + j0);
+        const float4 w1 = *reinterpret_cast<const float4*>(nw + j0 + 4);
+        v[0] *= inv * w0.x; v[1] *= inv * w0.y; v[2] *= inv * w0.z; v[3] *= inv * w0.w;
+        v[4] *= inv * w1.x; v[5] *= inv * w1.y; v[6] *= inv * w1.z; v[7] *= inv * w1.w;
+      }
+      if (rope) {
+        const float4 c = *reinterpret_cast<const float4*>(cs + (j0 >> 1));
+        const float4 s = *reinterpret_cast<const float4*>(sn + (j0 >> 1));
+        const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float a0 = v[2 * k], a1 = v[2 * k + 1];
+          v[2 * k] = a0 * cc[k] - a1 * ss[k];
+          v[2 * k + 1] = a0 * ss[k] + a1 * cc[k];
+        }
+      }
+      if (act_sig) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __fdividef(1.f, 1.f + __expf(-v[j]));
+      }
+      store_run<8>(dst, idx + j0, p.out_bf16, v);
+    }
+    return;
+  }
   auto val2 = [&](int j, float& a0, float& a1) {
     a0 = acc(j); a1 = acc(j + 1);
     if (nw) { a0 = a0 / rms * nw[j]; a1 = a1 / rms * nw[j + 1]; }
@@ -181,21 +235,12 @@ __device__ __forceinline__ void epi_head(const EpiParams& p, int m, int n0, cons
     }
     if (act_sig) { a0 = sigmoid_f(a0); a1 = sigmoid_f(a1); }
   };
-  if constexpr (HD > 0) {
-#pragma unroll
-    for (int j0 = 0; j0 < HD; j0 += 8) {
-      float v[8];
-#pragma unroll
-      for (int j = 0; j < 8; j += 2) val2(j0 + j, v[j], v[j + 1]);
-      store_run<8>(dst, idx + j0, p.out_bf16, v);
-    }
-  } else {
-    for (int j = 0; j < hd; j += 2) {
-      float a0, a1;
-      val2(j, a0, a1);
-      store_val(dst, idx + j, p.out_bf16, a0);
-      store_val(dst, idx + j + 1, p.out_bf16, a1);
-    }
+  // runtime-hd path (fp32 parity mode): the reference's exact divide order
+  for (int j = 0; j < hd; j += 2) {
+    float a0, a1;
+    val2(j, a0, a1);
+    store_val(dst, idx + j, p.out_bf16, a0);
+    store_val(dst, idx + j + 1, p.out_bf16, a1);
   }
 }
 

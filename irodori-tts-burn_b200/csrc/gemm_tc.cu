@@ -14,6 +14,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 #include <unordered_map>
 
@@ -162,7 +163,7 @@ struct Regs {
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
-                const __grid_constant__ EpiParams ep) {
+                int splits, const __grid_constant__ EpiParams ep) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -175,6 +176,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
   const int num_tiles = m_tiles * n_tiles;
   const int k_blocks = (K + BK - 1) / BK;
+  // work unit = (tile, K-split); splits > 1 only for the additive RESID epilogue
+  const int kpb = (k_blocks + splits - 1) / splits;
+  const int num_units = num_tiles * splits;
 
   auto full = [&](int s) { return smem_u32(&bars[s]); };
   auto empty = [&](int s) { return smem_u32(&bars[STAGES + s]); };
@@ -208,11 +212,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       uint32_t it = 0;
-      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+        const int t = u / splits, sp = u - t * splits;
+        const int kb0 = sp * kpb, kb1 = min(k_blocks, kb0 + kpb);
         int mi_, ni_;
         tile_coords(t, m_tiles, n_tiles, mi_, ni_);
         const int m0 = mi_ * BM, n0 = ni_ * BN;
-        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           mbar_wait(empty(s), ph ^ 1);
@@ -228,13 +234,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       uint32_t it = 0, tl = 0;
-      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tl) {
+      for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++tl) {
+        const int t = u / splits, sp = u - t * splits;
+        const int kb0 = sp * kpb, kb1 = min(k_blocks, kb0 + kpb);
         const int buf = tl & 1;
         const uint32_t aph = (tl >> 1) & 1;
         mbar_wait(tempty(buf), aph ^ 1);
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           mbar_wait(full(s), ph);
@@ -243,7 +251,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            umma_f16(d_tmem, sdesc(a_addr + kk * 32), sdesc(b_addr + kk * 32), C::IDESC, (kb | kk) != 0);
+            umma_f16(d_tmem, sdesc(a_addr + kk * 32), sdesc(b_addr + kk * 32), C::IDESC,
+                     (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           umma_commit(empty(s));  // frees the smem stage when these MMAs complete
         }
@@ -254,7 +263,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- epilogue warps 2..5 ----------------
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     uint32_t tl = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tl) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++tl) {
+      const int t = u / splits;
       const int buf = tl & 1;
       const uint32_t aph = (tl >> 1) & 1;
       int mi_, ni_;
@@ -291,7 +301,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_ld32(taddr, r0, c);
           tmem_ld32(taddr, r1, c + 32);
           tmem_wait_ld();
-          if (row_ok) epi_chunk_swiglu(ep, row, n0 + c, R);
+          if (row_ok) epi_chunk_swiglu<Regs<64>, true>(ep, row, n0 + c, R);
         }
       } else {
 #pragma unroll 1
@@ -301,7 +311,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_ld32(taddr, R.r, c);
           tmem_wait_ld();
           if (row_ok) {
-            if (ep.mode == EPI_RESID) epi_chunk_resid<32>(ep, row, n0 + c, R);
+            if (ep.mode == EPI_RESID) {
+              if (splits > 1) epi_chunk_resid_atomic<32>(ep, row, n0 + c, R);
+              else epi_chunk_resid<32>(ep, row, n0 + c, R);
+            }
             else epi_chunk_store<32>(ep, row, n0 + c, R);
           }
         }
@@ -388,20 +401,28 @@ int num_sms() {
 }
 
 template <int BN>
-void launch(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int K, const EpiParams& p,
+void launch(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int K, int splits, const EpiParams& p,
             cudaStream_t s) {
   using C = Cfg<BN>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static unsigned attr_mask = 0;  // per-device opt-in to the large dynamic smem
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_mask & (1u << (dev & 31)))) {
     IRT_CUDA(cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
-    attr_set = true;
+    attr_mask |= 1u << (dev & 31);
   }
   const CUtensorMap& ta = tensor_map(A, M, K, lda, BM);
   const CUtensorMap& tb = tensor_map(B, N, K, ldb, BN);
-  int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_kernel<BN><<<grid, THREADS, C::SMEM, s>>>(ta, tb, M, N, K, p);
+  int units = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * splits;
+  int grid = units < num_sms() ? units : num_sms();
+  gemm_kernel<BN><<<grid, THREADS, C::SMEM, s>>>(ta, tb, M, N, K, splits, p);
   IRT_CHECK_LAUNCH();
+}
+
+// Fraction of the SM-slots of the last wave that do useful work.
+double wave_eff(long units, int sms) {
+  long waves = (units + sms - 1) / sms;
+  return waves ? (double)units / (double)(waves * sms) : 0.0;
 }
 
 }  // namespace tc
@@ -417,11 +438,26 @@ bool gemm_tc_supported(const EpiParams& p, int K, long lda, long ldb, const void
 
 void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int K, const EpiParams& p,
              cudaStream_t s) {
-  // BN = 256 when it divides the per-head/segment structure, else 128.
+  // Tile width: 256 unless 128 fills the last wave clearly better (small M).
+  const int sms = tc::num_sms();
+  const long mt = (M + tc::BM - 1) / tc::BM;
+  const long t256 = mt * ((N + 255) / 256), t128 = mt * ((N + 127) / 128);
   bool use256 = N >= 256;
   if ((p.mode == EPI_QKVG || p.mode == EPI_CTXKV) && (p.Dq % 256)) use256 = false;
-  if (use256) tc::launch<256>(A, lda, B, ldb, M, N, K, p, s);
-  else tc::launch<128>(A, lda, B, ldb, M, N, K, p, s);
+  if (use256 && tc::wave_eff(t128, sms) > tc::wave_eff(t256, sms) + 0.1) use256 = false;
+  // K-splits for the additive residual epilogue when the tile count leaves
+  // SMs idle: each split keeps >= 8 k-blocks (512 of K).
+  int splits = 1;
+  const long tiles = use256 ? t256 : t128;
+  if (p.mode == EPI_RESID && !p.row_scale && tiles < sms) {
+    const int kb = (K + tc::BK - 1) / tc::BK;
+    splits = (int)std::min<long>((2L * sms) / tiles, kb / 8);
+    if (splits < 1) splits = 1;
+    const int kpb = (kb + splits - 1) / splits;
+    splits = (kb + kpb - 1) / kpb;  // no empty split
+  }
+  if (use256) tc::launch<256>(A, lda, B, ldb, M, N, K, splits, p, s);
+  else tc::launch<128>(A, lda, B, ldb, M, N, K, splits, p, s);
 }
 
 }  // namespace irt

@@ -115,6 +115,9 @@ void adaln_modulate(const float* x, const float* shift, const float* scale, void
                     float eps, cudaStream_t s);
 // y = x / sqrt(mean(x^2)+eps) * w   (RmsNorm; w may be null)
 void rms_norm(const float* x, const float* w, void* y, int out_bf16, int M, int D, float eps, cudaStream_t s);
+// out = RmsNorm(x; nw) . W^T + bias for a narrow output (W [P, D], bf16 or f32)
+void rmsnorm_proj(const float* x, const float* nw, const void* W, int w_bf16, const float* bias, float* out, int M,
+                  int D, int P, float eps, cudaStream_t s);
 // x[m] = table[ids[m]] * mask[m]
 void embed_rows(const int* ids, const uint8_t* mask, const float* table, float* x, int M, int D, cudaStream_t s);
 void embed_rows_v(const int* ids, const uint8_t* mask, const float* table, float* x, int M, int D, int vocab,

@@ -79,12 +79,118 @@ __global__ void __launch_bounds__(NT) rownorm_kernel(const float* __restrict__ x
   }
 }
 
+// Register-resident variant: each thread keeps up to VPT float4 of the row,
+// so the row is read from memory once.  Same arithmetic as rownorm_kernel.
+template <int NT, int VPT, bool OBF>
+__global__ void __launch_bounds__(NT) rownorm_reg_kernel(const float* __restrict__ x, const float* __restrict__ a,
+                                                         const float* __restrict__ b, void* __restrict__ y, int D,
+                                                         float eps, int mode) {
+  __shared__ float red[32];
+  const long row = blockIdx.x;
+  const int D4 = D >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * D);
+  float4 v[VPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = threadIdx.x + i * NT;
+    v[i] = c < D4 ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+  }
+  ss = block_sum<NT>(ss, red);
+  const float rms = sqrtf(ss / (float)D + eps);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = threadIdx.x + i * NT;
+    if (c >= D4) continue;
+    float o[4] = {v[i].x / rms, v[i].y / rms, v[i].z / rms, v[i].w / rms};
+    if (mode == 0) {
+      if (a) {
+        const float4 w = reinterpret_cast<const float4*>(a)[c];
+        o[0] *= w.x; o[1] *= w.y; o[2] *= w.z; o[3] *= w.w;
+      }
+    } else {
+      const float4 sh = reinterpret_cast<const float4*>(a)[c];
+      const float4 sc = reinterpret_cast<const float4*>(b)[c];
+      o[0] = o[0] * (sc.x + 1.f) + sh.x;
+      o[1] = o[1] * (sc.y + 1.f) + sh.y;
+      o[2] = o[2] * (sc.z + 1.f) + sh.z;
+      o[3] = o[3] * (sc.w + 1.f) + sh.w;
+    }
+    if (OBF) {
+      __nv_bfloat162 p0 = __floats2bfloat162_rn(o[0], o[1]), p1 = __floats2bfloat162_rn(o[2], o[3]);
+      uint2 u;
+      u.x = *reinterpret_cast<uint32_t*>(&p0);
+      u.y = *reinterpret_cast<uint32_t*>(&p1);
+      reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(y) + row * D)[c] = u;
+    } else {
+      reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + row * D)[c] = make_float4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 void rownorm(const float* x, const float* a, const float* b, void* y, int out_bf16, int M, int D, float eps, int mode,
              cudaStream_t s) {
   if (M <= 0) return;
-  if (out_bf16) rownorm_kernel<256, true><<<M, 256, 0, s>>>(x, a, b, y, D, eps, mode);
-  else rownorm_kernel<256, false><<<M, 256, 0, s>>>(x, a, b, y, D, eps, mode);
+  if ((D % 4) == 0 && D / 4 <= 256 * 2) {
+    if (out_bf16) rownorm_reg_kernel<256, 2, true><<<M, 256, 0, s>>>(x, a, b, y, D, eps, mode);
+    else rownorm_reg_kernel<256, 2, false><<<M, 256, 0, s>>>(x, a, b, y, D, eps, mode);
+  } else if (out_bf16) {
+    rownorm_kernel<256, true><<<M, 256, 0, s>>>(x, a, b, y, D, eps, mode);
+  } else {
+    rownorm_kernel<256, false><<<M, 256, 0, s>>>(x, a, b, y, D, eps, mode);
+  }
   IRT_CHECK_LAUNCH();
+}
+
+// out[m, n] = sum_d (x[m,d] / rms(x[m]) * nw[d]) * W[n, d] + bias[n]
+// (out_norm RmsNorm + out_proj Linear, src/model/dit/model.rs:391-392), one
+// warp per row, the normalised row staged once in shared memory, fp32 math.
+template <bool WBF>
+__global__ void __launch_bounds__(256) rmsnorm_proj_kernel(const float* __restrict__ x, const float* __restrict__ nw,
+                                                           const void* __restrict__ W, const float* __restrict__ bias,
+                                                           float* __restrict__ out, int M, int D, int P, float eps) {
+  extern __shared__ float xs_all[];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const long row = (long)blockIdx.x * (blockDim.x / 32) + warp;
+  float* xs = xs_all + warp * D;
+  if (row >= M) return;
+  const float* xr = x + row * D;
+  float ss = 0.f;
+  for (int d = lane; d < D; d += 32) ss += xr[d] * xr[d];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rms = sqrtf(ss / (float)D + eps);
+  for (int d = lane; d < D; d += 32) xs[d] = xr[d] / rms * nw[d];
+  __syncwarp();
+  // 8 outputs at a time: 8 independent weight-row loads in flight per step
+  constexpr int NB = 8;
+  for (int n0 = 0; n0 < P; n0 += NB) {
+    float acc[NB];
+#pragma unroll
+    for (int j = 0; j < NB; ++j) acc[j] = 0.f;
+    for (int d = lane; d < D; d += 32) {
+      const float xv = xs[d];
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        const int n = n0 + j < P ? n0 + j : P - 1;
+        const float wv = WBF ? __bfloat162float(reinterpret_cast<const bf16*>(W)[(long)n * D + d])
+                             : reinterpret_cast<const float*>(W)[(long)n * D + d];
+        acc[j] = fmaf(xv, wv, acc[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+    }
+    if (lane < NB && n0 + lane < P) {
+      float r = acc[0];
+#pragma unroll
+      for (int j = 1; j < NB; ++j) r = lane == j ? acc[j] : r;
+      out[row * P + n0 + lane] = r + (bias ? bias[n0 + lane] : 0.f);
+    }
+  }
 }
 
 __global__ void embed_kernel(const int* ids, const uint8_t* mask, const float* table, float* x, int M, int D,
@@ -226,6 +332,17 @@ void adaln_modulate(const float* x, const float* shift, const float* scale, void
 }
 void rms_norm(const float* x, const float* w, void* y, int out_bf16, int M, int D, float eps, cudaStream_t s) {
   rownorm(x, w, nullptr, y, out_bf16, M, D, eps, 0, s);
+}
+void rmsnorm_proj(const float* x, const float* nw, const void* W, int w_bf16, const float* bias, float* out, int M,
+                  int D, int P, float eps, cudaStream_t s) {
+  if (M <= 0) return;
+  if (D * 4 * 4 > 48 * 1024) throw unsupported("rmsnorm_proj: model_dim > 3072");
+  const int rows_per_block = 4;
+  const unsigned grid = (unsigned)((M + rows_per_block - 1) / rows_per_block);
+  const size_t smem = (size_t)rows_per_block * D * 4;
+  if (w_bf16) rmsnorm_proj_kernel<true><<<grid, 32 * rows_per_block, smem, s>>>(x, nw, W, bias, out, M, D, P, eps);
+  else rmsnorm_proj_kernel<false><<<grid, 32 * rows_per_block, smem, s>>>(x, nw, W, bias, out, M, D, P, eps);
+  IRT_CHECK_LAUNCH();
 }
 void embed_rows_v(const int* ids, const uint8_t* mask, const float* table, float* x, int M, int D, int vocab,
                   cudaStream_t s) {

@@ -146,6 +146,22 @@ def test_gemm_swiglu_and_resid(dev, path):
     assert err < 1e-4, f"resid rel err {err}"
 
 
+@pytest.mark.parametrize("M,N,K", [(300, 2048, 5888), (750, 2048, 2048), (1500, 2048, 5888)])
+def test_gemm_resid_split_k(dev, M, N, K):
+    """Few tiles -> the residual GEMM runs K-split with vector atomics; the
+    result must equal x + gate * (A @ W^T) (order-independent to fp32 rounding)."""
+    g = torch.Generator(device=dev).manual_seed(M + K)
+    A = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    W = (torch.randn(N, K, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    x = torch.randn(M, N, device=dev, generator=g)
+    gate = torch.randn(N, device=dev, generator=g)
+    ref = x + gate * (A.float() @ W.float().T)
+    check(hooks().irtt_gemm_epi(2, ptr(A), ptr(W), M, N, K, 0, None, None, None, None, None, None, None, None,
+                                None, 0, 0, 0, ptr(x), ptr(gate), 0))
+    err = (x - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-5, f"split-K resid rel err {err}"
+
+
 def _attn_ref(q, k, v, g, ck, cv, key_mask, seqs, H, hd):
     out = torch.zeros_like(q, dtype=torch.float32)
     for (ts, ln, co, cl) in seqs:
