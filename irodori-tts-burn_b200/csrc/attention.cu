@@ -334,7 +334,11 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnParams p) {
 
 void attention(const AttnParams& p, int bf16_io, cudaStream_t s) {
   if (p.nseq <= 0 || p.max_len <= 0) return;
-  if (bf16_io && p.hd == HD) {
+  if (bf16_io && p.path == 0 && attention_tc_supported(p)) {
+    attention_tc(p, s);
+    return;
+  }
+  if (bf16_io && p.hd == HD && p.path != 2) {
     static int attr_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);

@@ -398,6 +398,7 @@ void Engine::run_encoder(EncoderW& e, int B, int T, const void* input, bool from
     ap.nseq = B; ap.max_len = T; ap.H = e.heads; ap.hd = e.hd;
     ap.scale = 1.0f / std::sqrt((float)e.hd);
     ap.out = ws.eattn.p;
+    ap.rows = M;
     attention(ap, bf, s);
     EpiParams r;
     r.mode = EPI_RESID;
@@ -511,6 +512,8 @@ void Engine::dit_forward(int M, const SeqDesc* d_seqs, int nseq, int max_len, co
     ap.nseq = nseq; ap.max_len = max_len; ap.H = H; ap.hd = hd;
     ap.scale = 1.0f / std::sqrt((float)hd);
     ap.out = ws.attn.p;
+    ap.rows = M;
+    ap.ctx_rows = nrows_ctx;
     attention(ap, bf, s);
     EpiParams r;
     r.mode = EPI_RESID;
@@ -1100,7 +1103,7 @@ void Engine::sample(const irt_request& rq, float* out, int out_memory, cudaStrea
     IRT_CUDA(cudaMemcpyAsync(out, xs, nel * 4, okind, s));
   }
   IRT_CUDA(cudaStreamSynchronize(s));
-  if (read_and_clear_kernel_error())
+  if (read_and_clear_kernel_error() | read_and_clear_attn_error())
     throw Error(IRT_E_CUDA, "a GEMM pipeline wait timed out (device watchdog); results are invalid");
   last_launches = launch_counter().load() - launches0;
 }

@@ -42,7 +42,8 @@ struct Cfg {
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
-  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  // stages | barriers (256 B) | 4 x 32x33 f32 epilogue transpose buffers | alignment slack
+  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 256 + 4 * 32 * 33 * 4 + 1024;
   // instruction descriptor, kind::f16: D=f32 (bit4), A=B=bf16 (bits 7,10), K-major
   // both, N>>3 at bits 17-22, M>>4 at bits 24-28.
   static constexpr uint32_t IDESC =
@@ -303,6 +304,43 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_wait_ld();
           if (row_ok) epi_chunk_swiglu<Regs<64>, true>(ep, row, n0 + c, R);
         }
+      } else if (ep.mode == EPI_RESID) {
+        // Gated residual x += gate * acc through a per-warp 32x32 shared-memory
+        // transpose: lane l then owns column l, so every warp access to the f32
+        // residual stream is 128 contiguous bytes of one row (coalesced RMW).
+        float* stg = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES + 256) + quad * (32 * 33);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          if (n0 + c >= N) break;
+          Regs<32> R;
+          tmem_ld32(taddr, R.r, c);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) stg[lane * 33 + i] = R(i);
+          __syncwarp();
+          const int n = n0 + c + lane;
+          const bool col_ok = n < N;
+          const float g = (ep.gate && col_ok) ? ep.gate[n] : 1.f;
+          const int r0 = m0 + quad * 32;
+          float* xc = ep.x + n;
+          if (splits > 1) {
+#pragma unroll 8
+            for (int i = 0; i < 32; ++i)
+              if (col_ok && r0 + i < M) atomicAdd(xc + (long)(r0 + i) * N, g * stg[i * 33 + lane]);
+          } else {
+            float xv[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) xv[i] = (col_ok && r0 + i < M) ? xc[(long)(r0 + i) * N] : 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (col_ok && r0 + i < M) {
+                const float rs = ep.row_scale ? ep.row_scale[r0 + i] : 1.f;
+                xc[(long)(r0 + i) * N] = (xv[i] + g * stg[i * 33 + lane]) * rs;
+              }
+            }
+          }
+          __syncwarp();
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
@@ -310,13 +348,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           Regs<32> R;
           tmem_ld32(taddr, R.r, c);
           tmem_wait_ld();
-          if (row_ok) {
-            if (ep.mode == EPI_RESID) {
-              if (splits > 1) epi_chunk_resid_atomic<32>(ep, row, n0 + c, R);
-              else epi_chunk_resid<32>(ep, row, n0 + c, R);
-            }
-            else epi_chunk_store<32>(ep, row, n0 + c, R);
-          }
+          if (row_ok) epi_chunk_store<32>(ep, row, n0 + c, R);
         }
       }
       tc_fence_before();
@@ -411,8 +443,8 @@ void launch(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int 
     IRT_CUDA(cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
     attr_mask |= 1u << (dev & 31);
   }
-  const CUtensorMap& ta = tensor_map(A, M, K, lda, BM);
-  const CUtensorMap& tb = tensor_map(B, N, K, ldb, BN);
+  const CUtensorMap ta = tensor_map(A, M, K, lda, BM);  // copies: the cache may be cleared
+  const CUtensorMap tb = tensor_map(B, N, K, ldb, BN);
   int units = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * splits;
   int grid = units < num_sms() ? units : num_sms();
   gemm_kernel<BN><<<grid, THREADS, C::SMEM, s>>>(ta, tb, M, N, K, splits, p);
@@ -426,6 +458,11 @@ double wave_eff(long units, int sms) {
 }
 
 }  // namespace tc
+
+// bf16 2-D tensor map with a {64, box_rows} box and 128-byte swizzle (cached).
+const CUtensorMap& tma_map_bf16(const void* p, long rows, long cols, long ld, int box_rows) {
+  return tc::tensor_map(p, rows, cols, ld, box_rows);
+}
 
 bool gemm_tc_supported(const EpiParams& p, int K, long lda, long ldb, const void* A, const void* B) {
   if (K < tc::BK || (K % 8) || (lda % 8) || (ldb % 8)) return false;

@@ -103,8 +103,14 @@ struct AttnParams {
   int H, hd;
   float scale;
   void* out;          // [M, H*hd]
+  int rows;           // rows of the q/k/v buffers (TMA bounds)
+  int ctx_rows;       // rows of the context cache (TMA bounds)
+  int path;           // 0 = best available, 1 = mma.sync kernel, 2 = SIMT kernel
 };
 void attention(const AttnParams& p, int bf16_io, cudaStream_t s);
+bool attention_tc_supported(const AttnParams& p);
+void attention_tc(const AttnParams& p, cudaStream_t s);
+int read_and_clear_attn_error();
 
 // ---------------------------------------------------------------------------
 // Row-wise / elementwise kernels.  `T` selects bf16 (1) or f32 (0) storage

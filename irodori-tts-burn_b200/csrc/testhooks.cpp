@@ -87,7 +87,7 @@ IRTT_API int irtt_gemm_epi(int mode, const void* A, const void* B, int M, int N,
 // nseq x {tok_start, len, ctx_off, ctx_len}.
 IRTT_API int irtt_attention(const void* q, const void* k, const void* v, const void* g, const void* ck,
                             const void* cv, const uint8_t* key_mask, const int* seqs_host, int nseq, int H, int hd,
-                            void* out, int bf16_io) {
+                            void* out, int bf16_io, int rows, int ctx_rows, int path) {
   return guard([&] {
     std::vector<irt::SeqDesc> sd(nseq);
     int mx = 0;
@@ -103,8 +103,13 @@ IRTT_API int irtt_attention(const void* q, const void* k, const void* v, const v
     p.nseq = nseq; p.max_len = mx; p.H = H; p.hd = hd;
     p.scale = 1.0f / sqrtf((float)hd);
     p.out = out;
+    p.rows = rows;
+    p.ctx_rows = ctx_rows;
+    p.path = path;
+    if (path == 0 && bf16_io && !irt::attention_tc_supported(p)) throw irt::Error(4, "tcgen05 attention unsupported");
     irt::attention(p, bf16_io, nullptr);
     IRT_CUDA(cudaDeviceSynchronize());
+    if (irt::read_and_clear_attn_error()) throw irt::Error(20, "attention watchdog fired");
   });
 }
 

@@ -25,7 +25,8 @@ def hooks():
         L.irtt_gemm_store.argtypes = [ctypes.c_void_p] * 2 + [ctypes.c_int] * 3 + [ctypes.c_void_p, ctypes.c_int]
         L.irtt_gemm_epi.argtypes = ([ctypes.c_int] + [ctypes.c_void_p] * 2 + [ctypes.c_int] * 4 + [ctypes.c_void_p] * 9
                                     + [ctypes.c_int] * 3 + [ctypes.c_void_p] * 2 + [ctypes.c_int])
-        L.irtt_attention.argtypes = [ctypes.c_void_p] * 8 + [ctypes.c_int] * 3 + [ctypes.c_void_p, ctypes.c_int]
+        L.irtt_attention.argtypes = ([ctypes.c_void_p] * 8 + [ctypes.c_int] * 3 + [ctypes.c_void_p]
+                                     + [ctypes.c_int] * 4)
         _hooks = L
     return _hooks
 
@@ -183,29 +184,36 @@ def _attn_ref(q, k, v, g, ck, cv, key_mask, seqs, H, hd):
     return out
 
 
-@pytest.mark.parametrize("bf16", [1, 0])
-def test_attention_matches_torch(dev, bf16):
+ATTN_PATHS = [(1, 0), (1, 1), (0, 2)]  # (bf16, path): tcgen05, mma.sync, SIMT
+
+
+@pytest.mark.parametrize("bf16,path", ATTN_PATHS)
+@pytest.mark.parametrize("case", ["mixed", "config3"])
+def test_attention_matches_torch(dev, bf16, path, case):
     H, hd = 4, 128
     D = H * hd
-    seqs = [(0, 150, 0, 77), (150, 64, 77, 0), (214, 1, 77, 5), (215, 90, 82, 130)]
-    M = 305
-    nctx = 212
+    if case == "mixed":  # partial self tiles, empty / tiny / multi-tile contexts
+        seqs = [(0, 150, 0, 77), (150, 64, 77, 0), (214, 1, 77, 5), (215, 90, 82, 130)]
+        M, nctx = 305, 212
+    else:  # joint-CFG rows of config 3: cond (750 + 576 context keys), uncond (750 keys)
+        seqs = [(0, 750, 0, 576), (750, 750, 0, 0)]
+        M, nctx = 1500, 576
     dt = torch.bfloat16 if bf16 else torch.float32
     g = torch.Generator(device=dev).manual_seed(3)
     mk = lambda n: torch.randn(n, D, device=dev, generator=g).to(dt)
     q, k, v, ck, cv = mk(M), mk(M), mk(M), mk(nctx), mk(nctx)
     gs = torch.sigmoid(torch.randn(M, D, device=dev, generator=g)).to(dt)
     out = torch.zeros(M, D, device=dev, dtype=dt)
-    sd = (ctypes.c_int * 16)(*[x for s in seqs for x in s])
+    sd = (ctypes.c_int * (4 * len(seqs)))(*[x for s in seqs for x in s])
     check(hooks().irtt_attention(ptr(q), ptr(k), ptr(v), ptr(gs), ptr(ck), ptr(cv), None, sd, len(seqs), H, hd,
-                                 ptr(out), bf16))
+                                 ptr(out), bf16, M, nctx, path))
     ref = _attn_ref(q, k, v, gs, ck, cv, None, seqs, H, hd)
     err = (out.float() - ref).abs().max().item() / ref.abs().max().item()
     assert err < (2e-2 if bf16 else 1e-5), f"attention rel err {err}"
 
 
-@pytest.mark.parametrize("bf16", [1, 0])
-def test_attention_key_mask_and_empty_rows(dev, bf16):
+@pytest.mark.parametrize("bf16,path", [(1, 1), (0, 2)])
+def test_attention_key_mask_and_empty_rows(dev, bf16, path):
     """Masked self keys are skipped; a sequence whose keys are all masked
     yields exactly 0 (safe softmax), even with NaN in the masked V rows."""
     H, hd = 2, 128
@@ -224,7 +232,8 @@ def test_attention_key_mask_and_empty_rows(dev, bf16):
     seqs = [(0, 64, 0, 0), (64, 32, 0, 0)]
     out = torch.full((M, D), 7.0, device=dev, dtype=dt)
     sd = (ctypes.c_int * 8)(*[x for s in seqs for x in s])
-    check(hooks().irtt_attention(ptr(q), ptr(k), ptr(v), None, None, None, ptr(mask), sd, 2, H, hd, ptr(out), bf16))
+    check(hooks().irtt_attention(ptr(q), ptr(k), ptr(v), None, None, None, ptr(mask), sd, 2, H, hd, ptr(out), bf16,
+                                 M, 0, path))
     assert torch.isfinite(out.float()).all()
     assert (out[64:96].float() == 0).all()
     ref = _attn_ref(q, k, torch.nan_to_num(v), None, None, None, mask, seqs[:1], H, hd)
