@@ -194,6 +194,27 @@ IRT_API int irt_codec_hop_length(const irt_codec* c, int32_t* out);
 IRT_API int irt_codec_decode(irt_codec* c, const float* latent, int32_t batch, int32_t frames, float* wav,
                      int memory, void* stream);
 
+/*
+ * Allocation-free variant of irt_codec_decode.  No counterpart in the
+ * reference crate: it exists for callers that cannot allocate device memory
+ * during a decode -- a real-time streaming loop that cannot absorb the
+ * device-wide synchronisation of cudaMalloc/cudaFree, or a host application
+ * whose own allocator already holds the free HBM.  All intermediate
+ * activations live in one 16 MiB device array compiled into the library (held
+ * by every GPU that loads it until exit), so the call allocates nothing.
+ *   - latent [batch, frames, 32] and wav [batch, 1, frames * hop] must be
+ *     device (or managed) memory; the call returns once wav is complete.
+ *   - Capacity: batch * frames <= 7 latent frames (280 ms) for the full-width
+ *     DACVAE; larger requests fail with IRT_E_SHAPE and run nothing.
+ *   - The array is shared by every call on a device and keeps the last call's
+ *     contents (nothing in it needs to start at zero); calls that overlap on the
+ *     GPU race and must be serialised by the caller.
+ *   - The first call on a device resolves the array's address; make it before
+ *     any stream capture.
+ */
+IRT_API int irt_codec_decode_noalloc(irt_codec* c, const float* latent, int32_t batch, int32_t frames, float* wav,
+                                     void* stream);
+
 #ifdef __cplusplus
 }
 #endif

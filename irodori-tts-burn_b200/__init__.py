@@ -116,6 +116,8 @@ _SIGNATURES = {
     "irt_codec_hop_length": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32)]),
     "irt_codec_decode": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
                                         ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
+    "irt_codec_decode_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                                ctypes.c_void_p, ctypes.c_void_p]),
 }
 
 _lib = None
@@ -511,6 +513,24 @@ class DacVaeCodec:
         _check(lib().irt_codec_decode(self._h, ctypes.c_void_p(p), B, T, ctypes.c_void_p(o_p),
                                       MEM_DEVICE if dev else MEM_HOST, st))
         return res
+
+
+def decode_noalloc(codec: DacVaeCodec, latent, wav, stream=None):
+    """Allocation-free decode (``irt_codec_decode_noalloc``) for callers that
+    cannot allocate device memory mid-decode (streaming loops that cannot
+    absorb cudaMalloc/cudaFree synchronisation, hosts whose allocator owns the
+    free HBM).  ``latent`` [B, T, 32] and ``wav`` [B, 1, T * hop] are CUDA
+    tensors; B * T is limited by a fixed 16 MiB device scratch array (7 frames
+    for the full-width DACVAE).  Calls that overlap on the GPU race on that
+    array.  Returns ``wav``."""
+    B, T, C = latent.shape
+    if C != 32 or tuple(wav.shape) != (B, 1, T * codec.hop_length()):
+        raise IrodoriError(2, "Shape mismatch: latent [B, T, 32] and wav [B, 1, T * hop]")
+    lat = latent.contiguous()
+    st = ctypes.c_void_p(stream.cuda_stream) if stream is not None else None
+    _check(lib().irt_codec_decode_noalloc(codec._h, ctypes.c_void_p(lat.data_ptr()), B, T,
+                                          ctypes.c_void_p(wav.data_ptr()), st))
+    return wav
 
 
 def load_codec(path: str, device: int = 0, precision: str = "f32") -> DacVaeCodec:

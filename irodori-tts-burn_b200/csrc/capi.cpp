@@ -200,4 +200,14 @@ int irt_codec_decode(irt_codec* c, const float* latent, int32_t batch, int32_t f
   });
 }
 
+int irt_codec_decode_noalloc(irt_codec* c, const float* latent, int32_t batch, int32_t frames, float* wav,
+                             void* stream) {
+  return guard([&] {
+    need(c, "codec");
+    need(latent, "latent");
+    need(wav, "wav");
+    irt::codec_decode_noalloc(*c->c, latent, batch, frames, wav, reinterpret_cast<cudaStream_t>(stream));
+  });
+}
+
 }  // extern "C"

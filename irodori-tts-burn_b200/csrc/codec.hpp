@@ -38,4 +38,8 @@ struct Codec {
   void decode(const float* latent, int B, int T, float* wav, int memory, cudaStream_t s);
 };
 
+// Allocation-free decode into a fixed device scratch array (codec_noalloc.cu).
+void codec_decode_noalloc(Codec& c, const float* latent, int B, int T, float* wav, cudaStream_t s);
+size_t codec_noalloc_scratch_floats();
+
 }  // namespace irt
