@@ -365,6 +365,7 @@ def main():
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
     ap.add_argument("--skip-latency", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-config5", action="store_true")
     ap.add_argument("--ckpt", default=None)
     ap.add_argument("--latency-only", action="store_true",
                     help="only the config-3 single-utterance latency (used for profiling runs)")
@@ -456,6 +457,10 @@ def main():
     d2h = out_host.nbytes
     e2e_value = audio_total * args.steps / (e2e_ms / 1000.0)
 
+    c5 = None
+    if not args.skip_config5:
+        c5 = config5(pkg, eng, cfg, stream, rank, world, dist, max(1, min(args.steps, 3)), 1)
+
     if rank != 0:
         if dist is not None:
             dist.barrier()
@@ -495,12 +500,90 @@ def main():
             "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
-            "latency_config3": lat, **extra}
+            "latency_config3": lat, "config5": c5, **extra}
     print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+CODEC_CH = (1536, 768, 384, 192, 96)
+CODEC_RATES = (12, 10, 8, 2)
+
+
+def codec_flops_per_frame():
+    """Algorithmic FLOPs of the DACVAE decoder per latent frame: quantizer
+    out_proj, stem conv, per block the ConvTranspose (2 taps per output
+    sample) and 3 residual units (k7 conv + 1x1 conv), head conv."""
+    f = 2 * 32 * 1024 + 2 * 1024 * CODEC_CH[0] * 7
+    scale = 1
+    for i, s in enumerate(CODEC_RATES):
+        cin, cout = CODEC_CH[i], CODEC_CH[i + 1]
+        scale *= s
+        f += scale * (2 * 2 * cin * cout + 3 * (2 * 7 * cout * cout + 2 * cout * cout))
+    return f + scale * 2 * 7 * CODEC_CH[-1]
+
+
+def config5(pkg, eng, cfg, stream, rank, world, dist, steps, warmup):
+    """Config 5: config-4-style utterances (seed 5), 16 per GPU, sampled and
+    decoded to 48 kHz waveforms by the bf16 tensor-core DACVAE decoder
+    (reference-default random init).  Returns whole-job audio-s/s for
+    text -> waveform and for the decode alone (max over ranks)."""
+    import torch
+    import irodori_b200.synth as synth
+    utts = synth.throughput_utterances(16 * world, seed=5)
+    mine = list(range(16 * rank, 16 * rank + 16))
+    P = cfg["latent_dim"]
+    batch = build_batch(utts, mine, P, cfg["text_vocab_size"], seed=5)
+    keys = ("text_ids", "text_mask", "ref_latent", "ref_mask", "initial_noise")
+    dev_in = {k: batch[k].cuda() for k in keys}
+    B, Sm, lens = len(mine), batch["sequence_length"], batch["sequence_lengths"]
+    path = Path(tempfile.gettempdir()) / "irodori_bench" / f"codec_ref_init_r{rank}.safetensors"
+    path.parent.mkdir(parents=True, exist_ok=True)
+    if not path.exists():
+        synth.make_codec_checkpoint(str(path), seed=5, width_div=1, init="reference")
+    codec = pkg.load_codec(str(path), device=torch.cuda.current_device(), precision="bf16")
+    hop = codec.hop_length()
+    lat = torch.empty(B, Sm, P, device="cuda")
+    wav = torch.empty(B, 1, Sm * hop, device="cuda")
+    req = pkg.SamplingRequest(sequence_length=Sm, sequence_lengths=lens, **dev_in)
+
+    def step(decode_only):
+        if not decode_only:
+            eng.sample(req, out=lat, stream=stream)
+        codec.decode(lat, out=wav, stream=stream, lengths=lens)
+
+    def timed(decode_only, k):
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(k):
+            step(decode_only)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / k], device="cuda")
+        if dist is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(warmup):
+        step(False)
+    ms_t2w = timed(False, steps)
+    ms_dec = timed(True, steps)
+    audio_job = sum(u[3] for u in utts)
+    frames_rank = sum(lens)
+    dflops = codec_flops_per_frame() * frames_rank
+    return {"workload": "config5: 16 utterances per GPU (config-4 distribution, seed 5), sample + DACVAE decode, "
+                        "bf16, reference-default random codec init",
+            "scaling": "weak", "utterances": 16 * world, "audio_seconds": round(audio_job, 2),
+            "text_to_wave_audio_s_per_s": round(audio_job / (ms_t2w / 1000.0), 3),
+            "ms_per_step": round(ms_t2w, 2),
+            "decode_audio_s_per_s": round(audio_job / (ms_dec / 1000.0), 3), "decode_ms": round(ms_dec, 3),
+            "decode_tflops_rank0": round(dflops / (ms_dec / 1000.0) / 1e12, 1),
+            "decode_gflop_per_latent_frame": round(codec_flops_per_frame() / 1e9, 3)}
 
 
 def latency_only(args):

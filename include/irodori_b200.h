@@ -184,7 +184,9 @@ IRT_API int irt_engine_last_stats(const irt_engine* e, int64_t* row_forwards, in
 typedef struct irt_codec irt_codec;
 
 /* load_codec(path, device): decoder-path tensors of a weight-norm-resolved
- * DACVAE safetensors file (keys of src/codec/weights.rs:219-292). */
+ * DACVAE safetensors file (keys of src/codec/weights.rs:219-292).
+ * precision IRT_PREC_BF16: implicit-GEMM tcgen05 convolutions (bf16 operands,
+ * f32 accumulation and residual stream); IRT_PREC_F32: fp32 SIMT kernels. */
 IRT_API int irt_codec_create(int device, const char* safetensors_path, int precision, irt_codec** out);
 IRT_API int irt_codec_destroy(irt_codec* c);
 /* sample_rate() = 48000, hop_length() = 1920 (src/codec/model.rs:30-37). */
@@ -193,6 +195,14 @@ IRT_API int irt_codec_hop_length(const irt_codec* c, int32_t* out);
 /* DacVaeCodec::decode: latent [B, T, 32] -> wav [B, 1, T*1920]. */
 IRT_API int irt_codec_decode(irt_codec* c, const float* latent, int32_t batch, int32_t frames, float* wav,
                      int memory, void* stream);
+/* Ragged-batch extension of DacVaeCodec::decode (the reference decodes a
+ * padded batch as one tensor): utterance b has lengths[b] (host int32, 0 <=
+ * lengths[b] <= frames) valid latent frames and is decoded exactly as if it
+ * were decoded alone at that length; wav samples past lengths[b] * hop are 0.
+ * Used by batched text-to-waveform serving, where padding would be decoded
+ * and thrown away. */
+IRT_API int irt_codec_decode_ragged(irt_codec* c, const float* latent, int32_t batch, int32_t frames,
+                                    const int32_t* lengths, float* wav, int memory, void* stream);
 
 /*
  * Allocation-free variant of irt_codec_decode.  No counterpart in the

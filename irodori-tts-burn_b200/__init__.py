@@ -118,6 +118,9 @@ _SIGNATURES = {
                                         ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "irt_codec_decode_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
                                                 ctypes.c_void_p, ctypes.c_void_p]),
+    "irt_codec_decode_ragged": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                               ctypes.POINTER(ctypes.c_int32), ctypes.c_void_p, ctypes.c_int,
+                                               ctypes.c_void_p]),
 }
 
 _lib = None
@@ -490,8 +493,12 @@ class DacVaeCodec:
         _check(lib().irt_codec_hop_length(self._h, ctypes.byref(v)))
         return v.value
 
-    def decode(self, latent, out=None, stream=None):
-        """``[B, T, 32]`` latent -> ``[B, 1, T * hop_length]`` waveform."""
+    def decode(self, latent, out=None, stream=None, lengths=None):
+        """``[B, T, 32]`` latent -> ``[B, 1, T * hop_length]`` waveform.
+
+        ``lengths`` (extension, ``irt_codec_decode_ragged``): valid latent
+        frames per utterance; each utterance is decoded as if alone at its
+        length and samples past ``lengths[b] * hop_length`` are zero."""
         keep: list = []
         p, shape, dev = _as_buffer(latent, "float32", keep)
         if len(shape) != 3 or shape[2] != 32:
@@ -510,8 +517,16 @@ class DacVaeCodec:
             if o_mem != (MEM_DEVICE if dev else MEM_HOST):
                 raise IrodoriError(22, "latent and out must live in the same memory")
         st = ctypes.c_void_p(stream.cuda_stream) if stream is not None else None
-        _check(lib().irt_codec_decode(self._h, ctypes.c_void_p(p), B, T, ctypes.c_void_p(o_p),
-                                      MEM_DEVICE if dev else MEM_HOST, st))
+        if lengths is None:
+            _check(lib().irt_codec_decode(self._h, ctypes.c_void_p(p), B, T, ctypes.c_void_p(o_p),
+                                          MEM_DEVICE if dev else MEM_HOST, st))
+        else:
+            lens = [int(v) for v in lengths]
+            if len(lens) != B:
+                raise IrodoriError(2, f"Shape mismatch: {len(lens)} lengths for a batch of {B}")
+            arr = (ctypes.c_int32 * B)(*lens)
+            _check(lib().irt_codec_decode_ragged(self._h, ctypes.c_void_p(p), B, T, arr, ctypes.c_void_p(o_p),
+                                                 MEM_DEVICE if dev else MEM_HOST, st))
         return res
 
 

@@ -200,6 +200,17 @@ int irt_codec_decode(irt_codec* c, const float* latent, int32_t batch, int32_t f
   });
 }
 
+int irt_codec_decode_ragged(irt_codec* c, const float* latent, int32_t batch, int32_t frames, const int32_t* lengths,
+                            float* wav, int memory, void* stream) {
+  return guard([&] {
+    need(c, "codec");
+    need(latent, "latent");
+    need(lengths, "lengths");
+    need(wav, "wav");
+    c->c->decode(latent, batch, frames, wav, memory, reinterpret_cast<cudaStream_t>(stream), lengths);
+  });
+}
+
 int irt_codec_decode_noalloc(irt_codec* c, const float* latent, int32_t batch, int32_t frames, float* wav,
                              void* stream) {
   return guard([&] {

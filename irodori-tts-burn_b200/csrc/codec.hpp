@@ -3,16 +3,43 @@
 
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "common.hpp"
 #include "kernels.hpp"
 
 namespace irt {
 
+// One implicit-GEMM convolution launch of the bf16 tensor-core decoder
+// (conv_tc.cu).  A = bf16 rows [rows_in, cin]; weights packed bf16
+// [phases][cout][taps][cin_pad].
+struct ConvTcArgs {
+  int rows_in = 0, cin = 0, cin_pad = 0, taps = 1, phases = 1, cout = 0;
+  int dil = 1, pad = 0;         // conv1d: tap offset = tap * dil - pad
+  int convt = 0, stride = 1;    // ConvTranspose1d (kernel 2 * stride, padding pad)
+  int rows_out = 0;             // output rows
+  int out_scale = 1;            // output rows per latent frame
+  const int* frame_src = nullptr;  // per latent frame: utterance frame index, or -1 for a gap
+  const float* bias = nullptr;
+  const float* alpha = nullptr;    // Snake alpha applied to the bf16 output (nullptr: identity)
+  float* x = nullptr;              // f32 output rows [rows_out, cout] (nullptr: not written)
+  int add_res = 0;                 // x = x + conv (residual, in place)
+  bf16* p = nullptr;               // bf16 output rows [rows_out, cout] (nullptr: not written)
+};
+
+int conv_tc_bn(int cout);
+void conv_tc(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s);
+void pack_latent_rows(const float* lat, const int* frame_src, bf16* out, int F, cudaStream_t s);
+void codec_head_rows(const bf16* x, int R, int C, const float* w, const float* bias, int K, int pad,
+                     const int* frame_src, int hop, float* wav, cudaStream_t s);
+int conv_tc_read_and_clear_error();
+
 struct Codec {
   struct Conv {
     int cin = 0, cout = 0, k = 1, dil = 1, pad = 0;
     DevBuf w, b;
+    DevBuf wp;  // bf16 mode: packed [phases][cout][taps][cin_pad]
+    int cin_pad = 0, phases = 1;
   };
   struct Res {
     DevBuf a0, a2;
@@ -31,11 +58,21 @@ struct Codec {
   Block blocks[4];
   DevBuf head_alpha;
   DevBuf in, buf0, buf1, buf2;
+  // bf16 tensor-core path: row buffers and the frame table
+  bool tc = false;
+  DevBuf rx, rp, rq, frames, wav_dev;
   long long last_launches = 0;
 
   Codec(int dev, const std::string& path, int precision);
   ~Codec();
-  void decode(const float* latent, int B, int T, float* wav, int memory, cudaStream_t s);
+  // lengths: optional host array [B] of valid frames per utterance (ragged
+  // batch; samples past lengths[b] * hop are zero).  nullptr = all T frames.
+  void decode(const float* latent, int B, int T, float* wav, int memory, cudaStream_t s,
+              const int* lengths = nullptr);
+
+ private:
+  void pack_tc_weights();
+  void decode_tc(const float* latent_dev, int B, int T, const int* lengths, float* wav_dev, cudaStream_t s);
 };
 
 // Allocation-free decode into a fixed device scratch array (codec_noalloc.cu).

@@ -1,0 +1,395 @@
+// Implicit-GEMM tcgen05 convolutions for the DACVAE decoder in bf16 mode
+// (src/codec/decoder.rs:17-126, layers.rs:27-75).
+//
+// Activations are time-major bf16 rows [R, C] (channels contiguous).  A batch
+// is laid out as ONE time axis: every utterance is a run of latent frames with
+// GAP_FRAMES all-zero frames before, between and after the runs (the row
+// count at a decoder level is frames x upsampling so far).  The widest
+// receptive field at any level (kernel 7, dilation 9: 27 rows; ConvTranspose:
+// 1 input row) stays inside those zero rows, so "zero padding per utterance"
+// is just reading zero rows, and ragged batches cost nothing extra.  Every
+// epilogue writes exact zeros into gap rows; Snake(0) = 0 keeps them zero.
+//
+// conv1d (kernel k, dilation d, padding p):
+//   Y[t, co] = sum_tap sum_ci X[t + tap*d - p, ci] * W[co, ci, tap]
+//   = GEMM with M = t, N = co, K = (tap, ci); the A tile of k-block (tap, c0)
+//   is one TMA load of rows shifted by tap*d - p (rows outside [0, R) read the
+//   TMA zero fill).
+// ConvTranspose1d (kernel 2s, stride s, padding ceil(s/2), even or odd s >= 2):
+//   output o with o + pad = q*s + r receives exactly two taps,
+//   Y[o] = X[q] W[:, :, r] + X[q-1] W[:, :, r+s]; per phase r this is a 2-tap
+//   conv over q' = q - [r < pad] in [0, R_in), whose output rows are strided
+//   by s.  The phases are one more tile dimension of the same kernel.
+//
+// Persistent warp-specialised CTA (320 threads): warp 0 TMA producer, warp 1
+// TMEM allocator + tcgen05.mma issuer, warps 2..9 epilogue (two per TMEM lane
+// quadrant, alternate 32-column chunks) through a per-warp 32x33
+// shared-memory transpose so that every global access of a warp is one
+// contiguous run of a row (lane = output channel).  Two TMEM accumulators let
+// the epilogue of one tile overlap the MMAs of the next.  Every mbarrier wait
+// is bounded (watchdog flag, no hang).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "codec.hpp"
+#include "tc_common.cuh"
+
+namespace irt {
+
+// bf16 2-D tensor map, {64, box_rows} box, 128-byte swizzle (gemm_tc.cu).
+const CUtensorMap& tma_map_bf16(const void* p, long rows, long cols, long ld, int box_rows);
+
+namespace ctc {
+
+using namespace tcx;
+
+// warps 0 (TMA) and 1 (MMA) + EPI_WARPS epilogue warps; two epilogue warps
+// share each TMEM lane quadrant and split the 32-column chunks between them.
+constexpr int BM = 128, BK = 64, EPI_WARPS = 8, THREADS = 64 + 32 * EPI_WARPS;
+constexpr uint32_t A_BYTES = BM * BK * 2;
+
+template <int BN>
+struct Cfg {
+  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (184 * 1024) / STAGE_BYTES > 8 ? 8 : (184 * 1024) / STAGE_BYTES;
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
+  // second accumulator at a power-of-two column offset
+  static constexpr uint32_t ACC_STRIDE = TMEM_COLS / 2;
+  // alignment slack | stages | barriers (256 B) | one 32x33 f32 transpose buffer per epilogue warp
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256 + EPI_WARPS * 32 * 33 * 4;
+  static constexpr uint32_t IDESC = idesc_bf16(BM, BN);
+};
+
+// A-operand row offset of tap `tap` for output phase `phase`.
+__device__ __forceinline__ int a_row_off(const ConvTcArgs& a, int phase, int tap) {
+  return a.convt ? ((phase < a.pad ? 1 : 0) - tap) : (tap * a.dil - a.pad);
+}
+// Output row of GEMM row q in phase `phase`.
+__device__ __forceinline__ int out_row(const ConvTcArgs& a, int phase, int q) {
+  return a.convt ? (q + (phase < a.pad ? 1 : 0)) * a.stride + phase - a.pad : q;
+}
+
+// Snake with a precomputed 1 / (alpha + 1e-9); the hardware sine (MUFU) is
+// ample for a bf16 output.
+__device__ __forceinline__ float snake_inv(float v, float al, float inv) {
+  const float s = __sinf(al * v);
+  return v + s * s * inv;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(THREADS, 1)
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ ConvTcArgs a) {
+  using C = Cfg<BN>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  float* stage_f = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES + 256);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int m_tiles = (a.rows_in + BM - 1) / BM, n_tiles = a.cout / BN;
+  const int units = m_tiles * a.phases * n_tiles;
+  const int kpt = a.cin_pad / BK;  // k-blocks per tap
+  const int kbs = a.taps * kpt;
+
+  auto full = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty = [&](int s) { return smem_u32(&bars[STAGES + s]); };
+  auto tfull = [&](int b) { return smem_u32(&bars[2 * STAGES + b]); };
+  auto tempty = [&](int b) { return smem_u32(&bars[2 * STAGES + 2 + b]); };
+  // unit -> (m tile, phase, n tile); n innermost, then phase, so CTAs running
+  // at the same time share the A rows of one m tile through L2.
+  auto unit_coords = [&](int u, int& m_idx, int& phase, int& n_idx) {
+    n_idx = u % n_tiles;
+    const int r = u / n_tiles;
+    phase = r % a.phases;
+    m_idx = r / a.phases;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull(b), 1);
+      mbar_init(tempty(b), EPI_WARPS);
+    }
+    mbar_fence_init();
+    prefetch_map(&tmA);
+    prefetch_map(&tmB);
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        int mi, ph, ni;
+        unit_coords(u, mi, ph, ni);
+        const int m0 = mi * BM, n0 = ni * BN;
+        const int brow = ph * a.cout + n0;
+        for (int kb = 0; kb < kbs; ++kb, ++it) {
+          const int tap = kb / kpt, c0 = (kb - tap * kpt) * BK;
+          const int s = it % STAGES;
+          const uint32_t par = (it / STAGES) & 1;
+          mbar_wait(empty(s), par ^ 1);
+          uint8_t* a_dst = tiles + s * C::STAGE_BYTES;
+          mbar_expect_tx(full(s), C::STAGE_BYTES);
+          tma_load_2d(smem_u32(a_dst), &tmA, full(s), c0, m0 + a_row_off(a, ph, tap));
+          tma_load_2d(smem_u32(a_dst + A_BYTES), &tmB, full(s), tap * a.cin_pad + c0, brow);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t it = 0, tl = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x, ++tl) {
+        const int buf = tl & 1;
+        mbar_wait(tempty(buf), ((tl >> 1) & 1) ^ 1);
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * C::ACC_STRIDE;
+        for (int kb = 0; kb < kbs; ++kb, ++it) {
+          const int s = it % STAGES;
+          mbar_wait(full(s), (it / STAGES) & 1);
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(tiles + s * C::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_f16(d_tmem, sdesc_kmajor(a_addr + kk * 32), sdesc_kmajor(b_addr + kk * 32), C::IDESC,
+                     (kb | kk) ? 1u : 0u);
+          umma_commit(empty(s));  // frees the stage when these MMAs complete
+        }
+        umma_commit(tfull(buf));  // accumulator ready
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2 .. 2 + EPI_WARPS ----------------
+    const int quad = warp & 3;              // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) / 4;        // which 32-column chunks it takes
+    float* stg = stage_f + (warp - 2) * (32 * 33);
+    const int ostride = a.convt ? a.stride : 1;
+    uint32_t tl = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++tl) {
+      int mi, ph, ni;
+      unit_coords(u, mi, ph, ni);
+      const int m0 = mi * BM, n0 = ni * BN;
+      const int buf = tl & 1;
+      // lane l describes GEMM row q0 + l: whether its output row exists and
+      // whether it belongs to an utterance (else it is a gap row -> 0).
+      // Output rows of consecutive GEMM rows are ostride apart.
+      const int q0 = m0 + quad * 32;
+      const int o0 = out_row(a, ph, q0);
+      const int o = o0 + lane * ostride;
+      const bool ok = q0 + lane < a.rows_in && o >= 0 && o < a.rows_out;
+      const bool valid = ok && a.frame_src[o / a.out_scale] >= 0;
+      const unsigned okm = __ballot_sync(0xffffffffu, ok);
+      const unsigned vm = __ballot_sync(0xffffffffu, valid);
+      mbar_wait(tfull(buf), (tl >> 1) & 1);
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * C::ACC_STRIDE;
+#pragma unroll 1
+      for (int c = 32 * half; c < BN; c += 64) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) stg[lane * 33 + i] = __uint_as_float(r[i]);
+        __syncwarp();
+        const int co = n0 + c + lane;
+        const float bv = a.bias ? a.bias[co] : 0.f;
+        float al = 0.f, inv = 0.f;
+        if (a.alpha) {
+          al = a.alpha[co];
+          inv = 1.f / (al + 1e-9f);
+        }
+        const long col = co;
+        const long rstep = (long)ostride * a.cout;
+        const long base = (long)o0 * a.cout + col;
+        float xv[32];
+        if (a.add_res) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) xv[i] = ((okm >> i) & 1) ? a.x[base + i * rstep] : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (!((okm >> i) & 1)) continue;
+          float v = stg[i * 33 + lane] + bv;
+          if (a.add_res) v += xv[i];
+          if (!((vm >> i) & 1)) v = 0.f;
+          const long idx = base + i * rstep;
+          if (a.x) a.x[idx] = v;
+          if (a.p) a.p[idx] = __float2bfloat16_rn(a.alpha ? snake_inv(v, al, inv) : v);
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty(buf));
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Latent packing and the output head (SIMT: 32 -> 64 columns, 96 -> 1 channel)
+// ---------------------------------------------------------------------------
+
+// latent [B, T, 32] f32 -> rows [F, 64] bf16; frame f holds latent frame
+// frame_src[f] (b * T + t) or zeros for a gap frame; columns 32..63 are zero.
+__global__ void pack_latent_kernel(const float* __restrict__ lat, const int* __restrict__ frame_src,
+                                   __nv_bfloat16* __restrict__ out, int F) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)F * 64) return;
+  const int f = (int)(i / 64), c = (int)(i % 64);
+  const int src = frame_src[f];
+  out[i] = __float2bfloat16_rn((src >= 0 && c < 32) ? lat[(long)src * 32 + c] : 0.f);
+}
+
+// Head conv (src/codec/decoder.rs:43-54): wav = tanh(conv_k(Snake(x))) with the
+// Snake already applied by the producer of `x` (bf16 rows [R, C]).  One thread
+// per output row; rows of gap frames are skipped, utterance rows go to
+// wav[src * hop + (row % hop)].
+template <int C>
+__global__ void __launch_bounds__(256) head_kernel(const __nv_bfloat16* __restrict__ x, int R,
+                                                   const float* __restrict__ w, const float* __restrict__ bias, int K,
+                                                   int pad, const int* __restrict__ frame_src, int hop,
+                                                   float* __restrict__ wav) {
+  __shared__ float ws[7 * C];
+  for (int i = threadIdx.x; i < K * C; i += blockDim.x) {
+    const int k = i / C, c = i % C;
+    ws[i] = w[(long)c * K + k];  // weight [1, C, K]
+  }
+  __syncthreads();
+  const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= R) return;
+  const int src = frame_src[o / hop];
+  if (src < 0) return;
+  float acc = bias ? bias[0] : 0.f;
+  for (int k = 0; k < K; ++k) {
+    const int t = o + k - pad;
+    if (t < 0 || t >= R) continue;
+    const uint4* row = reinterpret_cast<const uint4*>(x + (long)t * C);
+#pragma unroll
+    for (int v = 0; v < C / 8; ++v) {
+      const uint4 u = row[v];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        acc = fmaf(f.x, ws[k * C + v * 8 + 2 * j], acc);
+        acc = fmaf(f.y, ws[k * C + v * 8 + 2 * j + 1], acc);
+      }
+    }
+  }
+  wav[(long)src * hop + (o % hop)] = tanhf(acc);
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN>
+void launch(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) {
+  using C = Cfg<BN>;
+  static unsigned attr_mask = 0;  // per-device opt-in to the large dynamic smem
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(attr_mask & (1u << (dev & 31)))) {
+      IRT_CUDA(cudaFuncSetAttribute(conv_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
+      attr_mask |= 1u << (dev & 31);
+    }
+  }
+  // copies: the map cache may be cleared by another thread
+  const CUtensorMap ta = tma_map_bf16(in, a.rows_in, a.cin, a.cin, BM);
+  const long kcols = (long)a.taps * a.cin_pad;
+  const CUtensorMap tb = tma_map_bf16(w, (long)a.phases * a.cout, kcols, kcols, BN);
+  const long units = (long)((a.rows_in + BM - 1) / BM) * a.phases * (a.cout / BN);
+  const int grid = (int)std::min<long>(units, num_sms());
+  conv_tc_kernel<BN><<<grid, THREADS, C::SMEM, s>>>(ta, tb, a);
+  IRT_CHECK_LAUNCH();
+}
+
+}  // namespace ctc
+
+int conv_tc_bn(int cout) {
+  for (int bn : {256, 192, 128, 96, 64, 32})
+    if (cout % bn == 0) return bn;
+  return 0;
+}
+
+void conv_tc(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) {
+  if (a.rows_in < ctc::BM || a.cin < 64 || (a.cin % 8) || (a.cin_pad % 64) || a.cin_pad < a.cin)
+    throw unsupported("conv_tc: input must have >= 128 rows and >= 64 channels (multiple of 8)");
+  if ((reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
+    throw unsupported("conv_tc: operands must be 16-byte aligned");
+  if ((long)a.rows_out * a.cout >= (1L << 31) || (long)a.rows_in * a.phases >= (1L << 31))
+    throw unsupported("conv_tc: level too large for 32-bit row indices");
+  switch (conv_tc_bn(a.cout)) {
+    case 256: ctc::launch<256>(in, w, a, s); break;
+    case 192: ctc::launch<192>(in, w, a, s); break;
+    case 128: ctc::launch<128>(in, w, a, s); break;
+    case 96: ctc::launch<96>(in, w, a, s); break;
+    case 64: ctc::launch<64>(in, w, a, s); break;
+    case 32: ctc::launch<32>(in, w, a, s); break;
+    default: throw unsupported("conv_tc: output channels must be a multiple of 32");
+  }
+}
+
+void pack_latent_rows(const float* lat, const int* frame_src, bf16* out, int F, cudaStream_t s) {
+  const long n = (long)F * 64;
+  if (!n) return;
+  ctc::pack_latent_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(lat, frame_src, out, F);
+  IRT_CHECK_LAUNCH();
+}
+
+void codec_head_rows(const bf16* x, int R, int C, const float* w, const float* bias, int K, int pad,
+                     const int* frame_src, int hop, float* wav, cudaStream_t s) {
+  if (K > 7) throw unsupported("codec head kernel > 7");
+  const unsigned grid = (unsigned)((R + 255) / 256);
+  switch (C) {
+    case 96: ctc::head_kernel<96><<<grid, 256, 0, s>>>(x, R, w, bias, K, pad, frame_src, hop, wav); break;
+    case 64: ctc::head_kernel<64><<<grid, 256, 0, s>>>(x, R, w, bias, K, pad, frame_src, hop, wav); break;
+    case 128: ctc::head_kernel<128><<<grid, 256, 0, s>>>(x, R, w, bias, K, pad, frame_src, hop, wav); break;
+    case 32: ctc::head_kernel<32><<<grid, 256, 0, s>>>(x, R, w, bias, K, pad, frame_src, hop, wav); break;
+    default: throw unsupported("codec head: channels must be 32, 64, 96 or 128");
+  }
+  IRT_CHECK_LAUNCH();
+}
+
+int conv_tc_read_and_clear_error() { return tcx::read_and_clear_flag(); }
+
+}  // namespace irt

@@ -163,20 +163,50 @@ __global__ void __launch_bounds__(256) rmsnorm_proj_kernel(const float* __restri
   const float rms = sqrtf(ss / (float)D + eps);
   for (int d = lane; d < D; d += 32) xs[d] = xr[d] / rms * nw[d];
   __syncwarp();
-  // 8 outputs at a time: 8 independent weight-row loads in flight per step
-  constexpr int NB = 8;
+  // 4 outputs at a time; each lane owns 8 consecutive columns per 256-column
+  // slab so weight rows are read with 16-byte (bf16) / 32-byte (f32) vectors.
+  constexpr int NB = 4;
+  const bool vec = (D % 256) == 0;
   for (int n0 = 0; n0 < P; n0 += NB) {
     float acc[NB];
 #pragma unroll
     for (int j = 0; j < NB; ++j) acc[j] = 0.f;
-    for (int d = lane; d < D; d += 32) {
-      const float xv = xs[d];
+    if (vec) {
+      for (int d0 = lane * 8; d0 < D; d0 += 256) {
+        const float4 x0 = *reinterpret_cast<const float4*>(xs + d0);
+        const float4 x1 = *reinterpret_cast<const float4*>(xs + d0 + 4);
+        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-      for (int j = 0; j < NB; ++j) {
-        const int n = n0 + j < P ? n0 + j : P - 1;
-        const float wv = WBF ? __bfloat162float(reinterpret_cast<const bf16*>(W)[(long)n * D + d])
-                             : reinterpret_cast<const float*>(W)[(long)n * D + d];
-        acc[j] = fmaf(xv, wv, acc[j]);
+        for (int j = 0; j < NB; ++j) {
+          const int n = n0 + j < P ? n0 + j : P - 1;
+          float wv[8];
+          if (WBF) {
+            const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(W) + (long)n * D + d0);
+            const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              wv[2 * k] = __bfloat162float(w2[k].x);
+              wv[2 * k + 1] = __bfloat162float(w2[k].y);
+            }
+          } else {
+            const float* wp = reinterpret_cast<const float*>(W) + (long)n * D + d0;
+            const float4 a = *reinterpret_cast<const float4*>(wp), b = *reinterpret_cast<const float4*>(wp + 4);
+            wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w; wv[4] = b.x; wv[5] = b.y; wv[6] = b.z; wv[7] = b.w;
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc[j] = fmaf(xv[k], wv[k], acc[j]);
+        }
+      }
+    } else {
+      for (int d = lane; d < D; d += 32) {
+        const float xv = xs[d];
+#pragma unroll
+        for (int j = 0; j < NB; ++j) {
+          const int n = n0 + j < P ? n0 + j : P - 1;
+          const float wv = WBF ? __bfloat162float(reinterpret_cast<const bf16*>(W)[(long)n * D + d])
+                               : reinterpret_cast<const float*>(W)[(long)n * D + d];
+          acc[j] = fmaf(xv, wv, acc[j]);
+        }
       }
     }
 #pragma unroll

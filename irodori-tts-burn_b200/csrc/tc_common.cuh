@@ -52,9 +52,12 @@ __device__ __forceinline__ uint64_t globaltimer() {
 }
 // Bounded wait: returns once the phase completes, or after ~4 s with the
 // watchdog flag set (the kernel then runs to completion with invalid data
-// instead of hanging the GPU).
+// instead of hanging the GPU).  Once the flag is set every later wait of this
+// translation unit's kernels gives up at once, so a stalled launch ends within
+// about one timeout rather than one per wait.
 __device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return;
+  if (*reinterpret_cast<volatile int*>(&g_watchdog)) return;
   const uint64_t t0 = globaltimer();
   for (;;) {
 #pragma unroll 1

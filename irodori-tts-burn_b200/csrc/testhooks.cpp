@@ -4,6 +4,7 @@
 #include <string>
 #include <vector>
 
+#include "codec.hpp"
 #include "common.hpp"
 #include "kernels.hpp"
 
@@ -120,5 +121,37 @@ IRTT_API int irtt_sync_check() {
   return guard([&] {
     IRT_CUDA(cudaDeviceSynchronize());
     if (irt::read_and_clear_kernel_error()) throw irt::Error(20, "pipeline watchdog fired");
+  });
+}
+
+// One implicit-GEMM convolution of the bf16 codec path (conv_tc.cu); all
+// pointers are device memory, w packed [phases][cout][taps][cin_pad] bf16.
+IRTT_API int irtt_conv_tc(const void* in, int rows_in, int cin, const void* w, int cin_pad, int taps, int phases,
+                          int cout, int dil, int pad, int convt, int stride, int rows_out, int out_scale,
+                          const int* frame_src, const float* bias, const float* alpha, float* x, int add_res,
+                          void* p) {
+  return guard([&] {
+    irt::ConvTcArgs a;
+    a.rows_in = rows_in;
+    a.cin = cin;
+    a.cin_pad = cin_pad;
+    a.taps = taps;
+    a.phases = phases;
+    a.cout = cout;
+    a.dil = dil;
+    a.pad = pad;
+    a.convt = convt;
+    a.stride = stride;
+    a.rows_out = rows_out;
+    a.out_scale = out_scale;
+    a.frame_src = frame_src;
+    a.bias = bias;
+    a.alpha = alpha;
+    a.x = x;
+    a.add_res = add_res;
+    a.p = reinterpret_cast<irt::bf16*>(p);
+    irt::conv_tc(reinterpret_cast<const irt::bf16*>(in), reinterpret_cast<const irt::bf16*>(w), a, nullptr);
+    IRT_CUDA(cudaDeviceSynchronize());
+    if (irt::conv_tc_read_and_clear_error()) throw irt::Error(20, "conv_tc watchdog fired");
   });
 }

@@ -240,11 +240,35 @@ def codec_param_shapes(width_div: int = 1) -> Dict[str, tuple]:
 
 
 def make_codec_checkpoint(path: str, seed: int = 5, width_div: int = 1,
-                          dtype: torch.dtype = torch.float32) -> None:
+                          dtype: torch.dtype = torch.float32, init: str = "weightnorm") -> None:
+    """Random decoder weights.
+
+    ``init="reference"``: the reference's own random initialisation of codec
+    layers (``Conv1dConfig::init`` in src/codec/encoder.rs:78-95: burn's
+    default Kaiming-uniform, weights and biases U(-1/sqrt(fan_in),
+    1/sqrt(fan_in)); Snake alpha = 1).  ``fan_in`` = in_channels x kernel for
+    Conv1d and out_channels x kernel for ConvTranspose1d ([in, out, k]).
+    ``init="weightnorm"``: weight-norm form g * v / |v| with g ~ U(0.5, 1.5)
+    per output row and alpha ~ U(1, 1.2) -- a stress case whose residual
+    stack amplifies input perturbations by a few hundred (fp32 parity only)."""
     gen = torch.Generator()
     gen.manual_seed(seed)
     tensors = {}
-    for name, shape in sorted(codec_param_shapes(width_div).items()):
+    shapes = codec_param_shapes(width_div)
+    if init == "reference":
+        for name, shape in sorted(shapes.items()):
+            if name.endswith(".alpha"):
+                t = torch.ones(shape)
+            else:
+                wname = name[:-len(".bias")] + ".weight" if name.endswith(".bias") else name
+                ws = shapes[wname]
+                fan_in = ws[1] * ws[2]  # dim 1 x kernel for both layouts
+                bound = 1.0 / math.sqrt(fan_in)
+                t = (torch.rand(shape, generator=gen) * 2 - 1) * bound
+            tensors[name] = t.to(dtype)
+        write_safetensors(path, tensors, {"config_json": json.dumps({})})
+        return
+    for name, shape in sorted(shapes.items()):
         if name.endswith(".alpha"):
             t = 1.0 + 0.2 * torch.rand(shape, generator=gen)
         elif name.endswith(".bias"):

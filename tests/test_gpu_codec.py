@@ -51,3 +51,81 @@ def test_codec_full_width_device_buffers(gpu, pkg, oracle, synth, tmp_path):
     codec.decode(lat.cuda(), out=out)
     err = rel_l2(out.cpu().numpy(), ref)
     assert err < 1e-4, err
+
+
+# ---------------------------------------------------------------------------
+# bf16 tensor-core decoder (implicit-GEMM tcgen05 convolutions)
+# ---------------------------------------------------------------------------
+
+# Waveform relative L2 bound for bf16 operands with f32 accumulation (40 dB
+# SNR).  Checked on the reference's own random initialisation of codec layers
+# (synth init="reference"); the weight-norm stress init amplifies any input
+# perturbation a few hundred times through its residual stack (fp32: 9e-5
+# against the oracle; bf16 rounding alone, emulated on the CPU: 0.24), so it
+# only serves the fp32 parity tests above.
+BF16_TOL = 1e-2
+
+
+def snr_db(out, ref):
+    out = np.asarray(out, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    return float(10 * np.log10(np.sum(ref ** 2) / max(np.sum((out - ref) ** 2), 1e-300)))
+
+
+@pytest.fixture(scope="module")
+def full_codec_path(tmp_path_factory, synth):
+    p = tmp_path_factory.mktemp("codec_tc") / "codec_full_ref_init.safetensors"
+    synth.make_codec_checkpoint(str(p), seed=5, width_div=1, init="reference")
+    return str(p)
+
+
+def test_codec_bf16_tc_matches_oracle(gpu, pkg, oracle, full_codec_path):
+    W = oracle.load_codec(full_codec_path)
+    lat = torch.randn(2, 6, 32, generator=torch.Generator().manual_seed(7))
+    ref = oracle.codec_decode(W, lat).numpy()
+    codec = pkg.load_codec(full_codec_path, device=0, precision="bf16")
+    out = codec.decode(lat)
+    assert out.shape == (2, 1, 6 * 1920)
+    assert np.isfinite(out).all()
+    err = rel_l2(out, ref)
+    print(f"bf16 codec vs oracle: rel L2 {err:.3e}, SNR {snr_db(out, ref):.1f} dB")
+    assert err < BF16_TOL, err
+
+
+def test_codec_f32_ragged_is_per_utterance(gpu, pkg, oracle, synth, tmp_path):
+    """Ragged decode = each utterance decoded alone at its length, zero tail."""
+    p = tmp_path / "codec_8.safetensors"
+    synth.make_codec_checkpoint(str(p), seed=5, width_div=8)
+    W = oracle.load_codec(str(p))
+    lat = torch.randn(3, 5, 32, generator=torch.Generator().manual_seed(9))
+    lens = [5, 2, 0]
+    codec = pkg.load_codec(str(p), device=0)
+    out = codec.decode(lat, lengths=lens)
+    for b, n in enumerate(lens):
+        if n:
+            ref = oracle.codec_decode(W, lat[b:b + 1, :n]).numpy()[0, 0]
+            assert rel_l2(out[b, 0, :n * 1920], ref) < 1e-4
+        assert not out[b, 0, n * 1920:].any()
+
+
+@pytest.mark.parametrize("B,T,lens", [(2, 150, None), (3, 200, [200, 57, 1]), (3, 3000, [3000, 1200, 100])])
+def test_codec_bf16_tc_matches_f32(gpu, pkg, full_codec_path, B, T, lens):
+    """Larger and ragged batches (the last case spans two decode chunks)
+    against the fp32 GPU decoder, itself checked against the oracle above."""
+    g = torch.Generator().manual_seed(B * 1000 + T)
+    lat = torch.randn(B, T, 32, generator=g).cuda()
+    hop = 1920
+    ref = torch.empty(B, 1, T * hop, device="cuda")
+    out = torch.full((B, 1, T * hop), float("nan"), device="cuda")
+    pkg.load_codec(full_codec_path, device=0, precision="f32").decode(lat, out=ref, lengths=lens)
+    pkg.load_codec(full_codec_path, device=0, precision="bf16").decode(lat, out=out, lengths=lens)
+    torch.cuda.synchronize()
+    lens = lens or [T] * B
+    for b, n in enumerate(lens):
+        o = out[b, 0].cpu().numpy()
+        r = ref[b, 0].cpu().numpy()
+        assert np.isfinite(o).all()
+        assert not o[n * hop:].any()
+        err = rel_l2(o[:n * hop], r[:n * hop])
+        print(f"B={B} T={T} utt {b} len {n}: rel L2 {err:.3e}, SNR {snr_db(o[:n * hop], r[:n * hop]):.1f} dB")
+        assert err < BF16_TOL, (b, err)
