@@ -366,6 +366,9 @@ def main():
     ap.add_argument("--skip-latency", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-config5", action="store_true")
+    ap.add_argument("--codec-only", action="store_true",
+                    help="time the config-5 DACVAE decode alone (16 utterances, seeded latents)")
+    ap.add_argument("--codec-precision", default="bf16", choices=["bf16", "f32"])
     ap.add_argument("--ckpt", default=None)
     ap.add_argument("--latency-only", action="store_true",
                     help="only the config-3 single-utterance latency (used for profiling runs)")
@@ -376,6 +379,8 @@ def main():
         return reference_arm(args)
     if args.latency_only:
         return latency_only(args)
+    if args.codec_only:
+        return codec_only(args)
     if args.gemm_case:
         import torch
         load_pkg()
@@ -584,6 +589,40 @@ def config5(pkg, eng, cfg, stream, rank, world, dist, steps, warmup):
             "decode_audio_s_per_s": round(audio_job / (ms_dec / 1000.0), 3), "decode_ms": round(ms_dec, 3),
             "decode_tflops_rank0": round(dflops / (ms_dec / 1000.0) / 1e12, 1),
             "decode_gflop_per_latent_frame": round(codec_flops_per_frame() / 1e9, 3)}
+
+
+def codec_only(args):
+    """Config-5 decode alone: the 16 utterance lengths of config 5 (rank 0,
+    seed 5) with N(0, 1) latents, bf16 tensor-core DACVAE decoder; prints one
+    JSON line (device buffers, CUDA-event time per decode)."""
+    import torch
+    pkg = load_pkg()
+    import irodori_b200.synth as synth
+    utts = synth.throughput_utterances(16, seed=5)
+    lens = [u[1] for u in utts]
+    T = max(lens)
+    path = Path(tempfile.gettempdir()) / "irodori_bench" / "codec_ref_init_r0.safetensors"
+    path.parent.mkdir(parents=True, exist_ok=True)
+    if not path.exists():
+        synth.make_codec_checkpoint(str(path), seed=5, width_div=1, init="reference")
+    codec = pkg.load_codec(str(path), device=0, precision=args.codec_precision)
+    lat = torch.randn(16, T, 32, generator=torch.Generator().manual_seed(5)).cuda()
+    wav = torch.empty(16, 1, T * codec.hop_length(), device="cuda")
+    for _ in range(args.warmup):
+        codec.decode(lat, out=wav, lengths=lens)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        codec.decode(lat, out=wav, lengths=lens)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    frames = sum(lens)
+    print(json.dumps({"codec_decode_ms": round(ms, 3), "precision": args.codec_precision, "frames": frames,
+                      "audio_s_per_s": round(frames / FRAME_RATE / (ms / 1000.0), 1),
+                      "tflops": round(codec_flops_per_frame() * frames / (ms / 1000.0) / 1e12, 1)}), flush=True)
+    return 0
 
 
 def latency_only(args):

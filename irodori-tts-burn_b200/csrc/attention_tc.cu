@@ -1,21 +1,26 @@
 // tcgen05 / TMEM flash attention for sm_100a (hd = 128, bf16 operands).
 //
-// One CTA = one (sequence, head, 128-query tile).  192 threads:
+// One CTA = one (sequence, head, 128-query tile).  320 threads:
 //   warp 0      TMA producer: Q once; per 128-key tile a K tile and a V tile,
 //               each on its own 2-stage ring (self keys first, then context)
 //   warp 1      TMEM allocator + single-thread MMA issuer:
 //                 S_j  = Q K_j^T       (M=128 queries, N=128 keys, K=128 hd) -> TMEM S[j&1]
-//                 O   += P_j V_j       (M=128, N=128 hd, K=128 keys; V MN-major) -> TMEM O
-//   warps 2..5  softmax: thread r owns query row r.  Per tile it loads the S
-//               row from TMEM (one batched wait), masks, takes the row max,
-//               writes P = exp2(s - m) as bf16 (128B-swizzled, K-major) to
-//               shared memory and keeps the row sum.  The running max is only
-//               raised when a row max grows by more than 2^8 (conditional
-//               rescale); then the warp rescales its O rows in TMEM after the
-//               previous P.V has completed.  Skipping is exact: O and l share
-//               the same stale max.
+//                 O_b += P_j V_j, b = j&1  (M=128, N=128 hd, K=128 keys; V MN-major)
+//   warps 2..9  two softmax warpgroups; group b takes key tiles j = b, b+2, ...
+//               with its own running max / sum and its own TMEM accumulator
+//               O_b, so the two groups' exponentials run concurrently.  Thread
+//               r of a group owns query row r.  Per tile it loads the S row
+//               from TMEM (one batched wait), masks, takes the row max, writes
+//               P = exp2(s - m) as bf16 (128B-swizzled, K-major) to shared
+//               memory and keeps the row sum.  The running max is only raised
+//               when a row max grows by more than 2^8 (conditional rescale);
+//               then the warp rescales its O_b rows in TMEM after the previous
+//               P.V into O_b has completed.  Skipping is exact: O_b and l_b
+//               share the same stale max.  At the end the groups exchange
+//               (m, l) through shared memory and each merges one 64-column
+//               half: O = (O_0 2^(m_0-m) + O_1 2^(m_1-m)) / (l_0 2^(m_0-m) + l_1 2^(m_1-m)).
 // Keys past a sequence's end get -inf scores; a row with no valid key outputs
-// 0.  Output = (O / l) * sigmoid-gate, bf16.
+// 0.  Output = O * sigmoid-gate, bf16.
 #include <algorithm>
 
 #include "common.hpp"
@@ -30,16 +35,21 @@ namespace {
 
 using namespace tcx;
 
-constexpr int QT = 128, KT = 128, HDIM = 128, THREADS = 192;
+constexpr int QT = 128, KT = 128, HDIM = 128, THREADS = 320;
 constexpr uint32_t TILE_BYTES = QT * HDIM * 2;  // 32 KB (two 16 KB 64-column halves)
 constexpr uint32_t HALF = TILE_BYTES / 2;
 // smem: Q | K0 K1 | V0 V1 | P0 P1 | barriers
 constexpr uint32_t OFF_Q = 0, OFF_K = TILE_BYTES, OFF_V = OFF_K + 2 * TILE_BYTES, OFF_P = OFF_V + 2 * TILE_BYTES;
 constexpr uint32_t OFF_BAR = OFF_P + 2 * TILE_BYTES;
 constexpr size_t SMEM = OFF_BAR + 256 + 1024;
+// (m, l) exchange of the final merge, [2 groups][m, l][128 rows] f32, in the Q
+// tile: once every group has seen its last P.V complete, every QK^T MMA
+// (issued before those P.V, and tracked by their commits) has finished
+// reading Q.
+constexpr uint32_t OFF_XCHG = OFF_Q;
 constexpr uint32_t IDESC_S = idesc_bf16(128, 128, false);
 constexpr uint32_t IDESC_O = idesc_bf16(128, 128, true);
-constexpr uint32_t TM_S = 0, TM_O = 256;  // TMEM columns: S double buffer, O accumulator
+constexpr uint32_t TM_S = 0, TM_O = 256;  // TMEM columns: S double buffer, O_0 | O_1 accumulators
 constexpr float RESCALE_LOG2 = 8.f;       // raise the running max only beyond 2^8 growth
 
 struct TcAttnArgs {
@@ -67,6 +77,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmCK,
                    const __grid_constant__ CUtensorMap tmCV, const __grid_constant__ TcAttnArgs a) {
+  pdl_wait();  // before any read of predecessor output, in every CTA
+  pdl_trigger();
   const SeqDesc sd = a.seqs[blockIdx.z];
   const int q0 = blockIdx.x * QT;
   if (q0 >= sd.len) return;
@@ -76,7 +88,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  const uint32_t Q_FULL = bar(0), O_DONE = bar(1);
+  const uint32_t Q_FULL = bar(0);
+  auto O_DONE = [&](int b) { return bar(18 + b); };
   auto K_FULL = [&](int s) { return bar(2 + s); };
   auto K_EMPTY = [&](int s) { return bar(4 + s); };
   auto V_FULL = [&](int s) { return bar(6 + s); };
@@ -85,7 +98,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   auto S_EMPTY = [&](int b) { return bar(12 + b); };
   auto P_FULL = [&](int b) { return bar(14 + b); };
   auto P_EMPTY = [&](int b) { return bar(16 + b); };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_self = (sd.len + KT - 1) / KT;
@@ -94,8 +107,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(Q_FULL, 1);
-    mbar_init(O_DONE, 1);
     for (int b = 0; b < 2; ++b) {
+      mbar_init(O_DONE(b), 1);
       mbar_init(K_FULL(b), 1);
       mbar_init(K_EMPTY(b), 1);
       mbar_init(V_FULL(b), 1);
@@ -180,21 +193,24 @@ __global__ void __launch_bounds__(THREADS, 1)
           // halves 16 KB apart, 8-key groups 1 KB apart)
           const uint32_t aoff = (kk >> 2) * HALF + (kk & 3) * 32;
           const uint64_t bdesc = sdesc_sw128(sV(s) + kk * 16 * 128, HALF, 1024);
-          umma_f16(tmem + TM_O, sdesc_kmajor(sP(s) + aoff), bdesc, IDESC_O, (j | kk) != 0);
+          umma_f16(tmem + TM_O + s * 128, sdesc_kmajor(sP(s) + aoff), bdesc, IDESC_O, (j >= 2 || kk != 0));
         }
         umma_commit(P_EMPTY(s));
         umma_commit(V_EMPTY(s));
-        umma_commit(O_DONE);  // one phase per tile
+        umma_commit(O_DONE(s));  // one phase per tile of group s
       }
     }
   } else {
-    // ---------------- softmax warps ----------------
+    // ---------------- softmax warps: two groups ----------------
     const int quad = warp & 3;
+    const int grp = (warp - 2) >> 2;   // group: key tiles j = grp, grp + 2, ...
     const int row = quad * 32 + lane;  // query row within the tile
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t o_col = TM_O + grp * 128;
     float m_run = -INFINITY, l_run = 0.f;
-    for (int j = 0; j < ntiles; ++j) {
-      const int b = j & 1;
+    int last = -1;
+    for (int j = grp; j < ntiles; j += 2) {
+      const int b = grp;  // == j & 1
       const bool self = j < n_self;
       const int kvalid = (self ? sd.len - j * KT : sd.ctx_len - (j - n_self) * KT);  // valid keys in tile
       mbar_wait(S_FULL(b), (j >> 1) & 1);
@@ -242,18 +258,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         *reinterpret_cast<uint4*>(prow + sub * HALF + ((cin ^ (row & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       l_run = l_run * corr + rsum;
-      // Rescale O (warp-collective) once the previous P.V is complete.
-      if (__any_sync(0xffffffffu, raise) && j > 0) {
-        mbar_wait(O_DONE, (j - 1) & 1);
+      // Rescale O_b (warp-collective) once the previous P.V into O_b is complete.
+      if (__any_sync(0xffffffffu, raise) && j >= 2) {
+        mbar_wait(O_DONE(b), ((j >> 1) - 1) & 1);
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < HDIM / 32; ++c) {
           uint32_t r[32];
-          tmem_ld32(tmem + lane_off + TM_O + c * 32, r);
+          tmem_ld32(tmem + lane_off + o_col + c * 32, r);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
-          tmem_st32(tmem + lane_off + TM_O + c * 32, r);
+          tmem_st32(tmem + lane_off + o_col + c * 32, r);
         }
         tmem_wait_st();
       }
@@ -261,18 +277,36 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(P_FULL(b));
+      last = j;
     }
-
-    // epilogue: wait for the last P.V, O / l, gate, bf16 store of this row
-    if (ntiles > 0) mbar_wait(O_DONE, (ntiles - 1) & 1);
+    // this group's last P.V into O_grp
+    if (last >= 0) mbar_wait(O_DONE(grp), (last >> 1) & 1);
     tc_fence_after();
+
+    // merge the two groups: exchange (m, l) per row, each group finishes one
+    // 64-column half of hd from both accumulators.  The first barrier (the 8
+    // softmax warps) orders the exchange writes into the Q tile after every
+    // group's final wait: a group without tiles has waited for nothing.
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    float* xg = reinterpret_cast<float*>(sm + OFF_XCHG);
+    xg[(grp * 2 + 0) * 128 + row] = last >= 0 ? m_run : -INFINITY;
+    xg[(grp * 2 + 1) * 128 + row] = last >= 0 ? l_run : 0.f;
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    const float m0 = xg[0 * 128 + row], l0 = xg[1 * 128 + row];
+    const float m1 = xg[2 * 128 + row], l1 = xg[3 * 128 + row];
+    const float mm = fmaxf(m0, m1);
+    const float c0 = (mm == -INFINITY || l0 == 0.f) ? 0.f : ex2(m0 - mm);
+    const float c1 = (mm == -INFINITY || l1 == 0.f) ? 0.f : ex2(m1 - mm);
+    const float lsum = l0 * c0 + l1 * c1;
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    const float w0 = c0 * inv, w1 = c1 * inv;
     const int qi = q0 + row;
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
     const long off = (long)(sd.tok_start + (qi < sd.len ? qi : 0)) * D + h * HDIM;
 #pragma unroll 1
-    for (int c = 0; c < HDIM / 32; ++c) {
-      uint32_t r[32];
-      tmem_ld32(tmem + lane_off + TM_O + c * 32, r);
+    for (int c = grp * 2; c < grp * 2 + 2; ++c) {
+      uint32_t r0[32], r1[32];
+      tmem_ld32(tmem + lane_off + TM_O + c * 32, r0);
+      tmem_ld32(tmem + lane_off + TM_O + 128 + c * 32, r1);
       tmem_wait_ld();
       if (qi < sd.len) {
 #pragma unroll
@@ -293,8 +327,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint32_t op[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            __nv_bfloat162 t = __floats2bfloat162_rn(__uint_as_float(r[d0 + 2 * k]) * inv * g[2 * k],
-                                                     __uint_as_float(r[d0 + 2 * k + 1]) * inv * g[2 * k + 1]);
+            float v[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int d = d0 + 2 * k + e;
+              // an accumulator that received no tile is never read (w == 0)
+              const float o0 = w0 != 0.f ? __uint_as_float(r0[d]) * w0 : 0.f;
+              const float o1 = w1 != 0.f ? __uint_as_float(r1[d]) * w1 : 0.f;
+              v[e] = (o0 + o1) * g[2 * k + e];
+            }
+            __nv_bfloat162 t = __floats2bfloat162_rn(v[0], v[1]);
             op[k] = *reinterpret_cast<uint32_t*>(&t);
           }
           *reinterpret_cast<uint4*>(a.out + off + c * 32 + d0) = make_uint4(op[0], op[1], op[2], op[3]);
@@ -351,7 +393,7 @@ void attention_tc(const AttnParams& p, cudaStream_t s) {
   a.H = p.H;
   a.scale_log2 = p.scale * 1.4426950408889634f;
   dim3 grid((p.max_len + QT - 1) / QT, p.H, p.nseq);
-  attn_tc_kernel<<<grid, THREADS, SMEM, s>>>(mq, mk, mv, mck, mcv, a);
+  launch_pdl(attn_tc_kernel, grid, dim3(THREADS), SMEM, s, mq, mk, mv, mck, mcv, a);
   IRT_CHECK_LAUNCH();
 }
 

@@ -8,9 +8,11 @@
 #include <atomic>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 #include "../../include/irodori_b200.h"
 
@@ -50,6 +52,42 @@ inline std::atomic<long long>& launch_counter() {
     ::irt::launch_counter().fetch_add(1, std::memory_order_relaxed); \
     IRT_CUDA(cudaGetLastError());                              \
   } while (0)
+
+// Programmatic dependent launch (PDL).  A kernel launched with launch_pdl()
+// may start while its predecessor on the stream is still running; it must
+// execute pdl_wait() in every CTA before it reads anything a predecessor
+// wrote (pdl_wait returns once the predecessor grid has completed and its
+// memory is visible, so ordering stays transitive).  pdl_trigger() lets the
+// successor grid launch early; it never weakens the successor's own wait.
+// Both are no-ops for kernels launched the ordinary way.  IRT_NO_PDL=1 in the
+// environment launches everything the ordinary way.
+#if defined(__CUDACC__)
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("IRT_NO_PDL");
+    return !(e && e[0] == '1');
+  }();
+  return on;
+}
+
+template <class... KArgs, class... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  IRT_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+#endif
 
 // Owning device allocation (cudaMalloc / cudaFree).
 struct DevBuf {

@@ -131,6 +131,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the prologue above may overlap the previous kernel; operands are read only now
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -339,7 +342,7 @@ void launch(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) 
   const CUtensorMap tb = tma_map_bf16(w, (long)a.phases * a.cout, kcols, kcols, BN);
   const long units = (long)((a.rows_in + BM - 1) / BM) * a.phases * (a.cout / BN);
   const int grid = (int)std::min<long>(units, num_sms());
-  conv_tc_kernel<BN><<<grid, THREADS, C::SMEM, s>>>(ta, tb, a);
+  launch_pdl(conv_tc_kernel<BN>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, a);
   IRT_CHECK_LAUNCH();
 }
 

@@ -3,10 +3,12 @@
 //   C[M,N] = A[M,K] . B[N,K]^T   (A activations, B PyTorch-layout weights;
 //                                 both K-major, bf16; fp32 accumulate in TMEM)
 //
-// Persistent, warp-specialised CTA of 192 threads:
+// Persistent, warp-specialised CTA of 320 threads:
 //   warp 0      TMA producer: A tile 128x64 and B tile BNx64 per stage (128B swizzle)
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16)
-//   warps 2..5  epilogue: tcgen05.ld 32x32b -> registers -> fused epilogue -> global
+//   warps 2..9  epilogue: tcgen05.ld 32x32b -> registers -> fused epilogue -> global;
+//               two warps per TMEM lane quadrant split the tile's columns (one
+//               128-column head each for QKVG, alternate chunks otherwise)
 // Two TMEM accumulator buffers let the epilogue of tile i overlap the MMAs of
 // tile i+1.  Tiles are walked in grouped order (see tile_coords).  Every
 // mbarrier wait is bounded by a 4 s watchdog that sets a device error flag
@@ -34,7 +36,7 @@ int read_and_clear_kernel_error() {
 
 namespace tc {
 
-constexpr int BM = 128, BK = 64, STAGES = 4, THREADS = 192;
+constexpr int BM = 128, BK = 64, STAGES = 4, EPI_WARPS = 8, THREADS = 64 + 32 * EPI_WARPS;
 constexpr uint32_t A_BYTES = BM * BK * 2;
 
 template <int BN>
@@ -42,8 +44,8 @@ struct Cfg {
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
-  // stages | barriers (256 B) | 4 x 32x33 f32 epilogue transpose buffers | alignment slack
-  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 256 + 4 * 32 * 33 * 4 + 1024;
+  // stages | barriers (256 B) | one 32x33 f32 transpose buffer per epilogue warp | alignment slack
+  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 256 + EPI_WARPS * 32 * 33 * 4 + 1024;
   // instruction descriptor, kind::f16: D=f32 (bit4), A=B=bf16 (bits 7,10), K-major
   // both, N>>3 at bits 17-22, M>>4 at bits 24-28.
   static constexpr uint32_t IDESC =
@@ -162,6 +164,8 @@ struct Regs {
 };
 
 template <int BN>
+// 320 threads: registers are budgeted per 4-warp group, so 10 warps cost as
+// much as 12 and the kernel must stay at or below 168 registers per thread.
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
                 int splits, const __grid_constant__ EpiParams ep) {
@@ -193,7 +197,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull(b), 1);
-      mbar_init(tempty(b), 4);
+      mbar_init(tempty(b), EPI_WARPS);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
@@ -208,6 +212,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the prologue above may overlap the previous kernel; operands are read only now
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -261,8 +268,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue warps 2..5 ----------------
-    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    // ---------------- epilogue warps 2 .. 2 + EPI_WARPS ----------------
+    const int quad = warp & 3;       // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) / 4;  // which columns of the tile it takes
     uint32_t tl = 0;
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++tl) {
       const int t = u / splits;
@@ -278,7 +286,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * BN;
       if (ep.mode == EPI_QKVG || ep.mode == EPI_CTXKV) {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 128) {
+        for (int c = 128 * half; c < BN; c += 256) {
           if (n0 + c >= N) break;
           Regs<128> R;
           uint32_t(&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&R.r[0]);
@@ -294,7 +302,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       } else if (ep.mode == EPI_SWIGLU) {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 64) {
+        for (int c = 64 * half; c < BN; c += 128) {
           if (n0 + c >= N) break;
           Regs<64> R;
           uint32_t(&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&R.r[0]);
@@ -308,9 +316,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         // Gated residual x += gate * acc through a per-warp 32x32 shared-memory
         // transpose: lane l then owns column l, so every warp access to the f32
         // residual stream is 128 contiguous bytes of one row (coalesced RMW).
-        float* stg = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES + 256) + quad * (32 * 33);
+        float* stg = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES + 256) + (warp - 2) * (32 * 33);
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = 32 * half; c < BN; c += 64) {
           if (n0 + c >= N) break;
           Regs<32> R;
           tmem_ld32(taddr, R.r, c);
@@ -343,7 +351,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = 32 * half; c < BN; c += 64) {
           if (n0 + c >= N) break;
           Regs<32> R;
           tmem_ld32(taddr, R.r, c);
@@ -447,7 +455,7 @@ void launch(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int 
   const CUtensorMap tb = tensor_map(B, N, K, ldb, BN);
   int units = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * splits;
   int grid = units < num_sms() ? units : num_sms();
-  gemm_kernel<BN><<<grid, THREADS, C::SMEM, s>>>(ta, tb, M, N, K, splits, p);
+  launch_pdl(gemm_kernel<BN>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, M, N, K, splits, p);
   IRT_CHECK_LAUNCH();
 }
 

@@ -35,6 +35,8 @@ template <int NT, bool OBF>
 __global__ void __launch_bounds__(NT) rownorm_kernel(const float* __restrict__ x, const float* __restrict__ a,
                                                      const float* __restrict__ b, void* __restrict__ y, int D,
                                                      float eps, int mode) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   const long row = blockIdx.x;
   const float* xr = x + row * D;
@@ -85,6 +87,8 @@ template <int NT, int VPT, bool OBF>
 __global__ void __launch_bounds__(NT) rownorm_reg_kernel(const float* __restrict__ x, const float* __restrict__ a,
                                                          const float* __restrict__ b, void* __restrict__ y, int D,
                                                          float eps, int mode) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   const long row = blockIdx.x;
   const int D4 = D >> 2;
@@ -133,12 +137,12 @@ void rownorm(const float* x, const float* a, const float* b, void* y, int out_bf
              cudaStream_t s) {
   if (M <= 0) return;
   if ((D % 4) == 0 && D / 4 <= 256 * 2) {
-    if (out_bf16) rownorm_reg_kernel<256, 2, true><<<M, 256, 0, s>>>(x, a, b, y, D, eps, mode);
-    else rownorm_reg_kernel<256, 2, false><<<M, 256, 0, s>>>(x, a, b, y, D, eps, mode);
+    if (out_bf16) launch_pdl(rownorm_reg_kernel<256, 2, true>, dim3(M), dim3(256), 0, s, x, a, b, y, D, eps, mode);
+    else launch_pdl(rownorm_reg_kernel<256, 2, false>, dim3(M), dim3(256), 0, s, x, a, b, y, D, eps, mode);
   } else if (out_bf16) {
-    rownorm_kernel<256, true><<<M, 256, 0, s>>>(x, a, b, y, D, eps, mode);
+    launch_pdl(rownorm_kernel<256, true>, dim3(M), dim3(256), 0, s, x, a, b, y, D, eps, mode);
   } else {
-    rownorm_kernel<256, false><<<M, 256, 0, s>>>(x, a, b, y, D, eps, mode);
+    launch_pdl(rownorm_kernel<256, false>, dim3(M), dim3(256), 0, s, x, a, b, y, D, eps, mode);
   }
   IRT_CHECK_LAUNCH();
 }
@@ -150,6 +154,8 @@ template <bool WBF>
 __global__ void __launch_bounds__(256) rmsnorm_proj_kernel(const float* __restrict__ x, const float* __restrict__ nw,
                                                            const void* __restrict__ W, const float* __restrict__ bias,
                                                            float* __restrict__ out, int M, int D, int P, float eps) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float xs_all[];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const long row = (long)blockIdx.x * (blockDim.x / 32) + warp;
@@ -370,8 +376,12 @@ void rmsnorm_proj(const float* x, const float* nw, const void* W, int w_bf16, co
   const int rows_per_block = 4;
   const unsigned grid = (unsigned)((M + rows_per_block - 1) / rows_per_block);
   const size_t smem = (size_t)rows_per_block * D * 4;
-  if (w_bf16) rmsnorm_proj_kernel<true><<<grid, 32 * rows_per_block, smem, s>>>(x, nw, W, bias, out, M, D, P, eps);
-  else rmsnorm_proj_kernel<false><<<grid, 32 * rows_per_block, smem, s>>>(x, nw, W, bias, out, M, D, P, eps);
+  if (w_bf16)
+    launch_pdl(rmsnorm_proj_kernel<true>, dim3(grid), dim3(32 * rows_per_block), smem, s, x, nw, W, bias, out, M, D, P,
+               eps);
+  else
+    launch_pdl(rmsnorm_proj_kernel<false>, dim3(grid), dim3(32 * rows_per_block), smem, s, x, nw, W, bias, out, M, D,
+               P, eps);
   IRT_CHECK_LAUNCH();
 }
 void embed_rows_v(const int* ids, const uint8_t* mask, const float* table, float* x, int M, int D, int vocab,
