@@ -249,6 +249,47 @@ def gemm_roofline(M, reps=5):
 # CPU leg: the oracle (restatement of the reference path) on the host cores
 # ---------------------------------------------------------------------------
 
+def attn_case(steps):
+    """Profiling case: the joint attention of one DiT layer at the config-3
+    CFG step (cond row: 750 queries over 750 self + 576 context keys; uncond
+    row: 750 over 750), H = 16, hd = 128, bf16, through the tcgen05 kernel;
+    `steps` launches timed with CUDA events.  Returns (ms per launch, TFLOP/s)."""
+    import torch
+    L = ctypes.CDLL(str(PKG_DIR / "libirodori_b200_testhooks.so"))
+    L.irtt_attention.argtypes = ([ctypes.c_void_p] * 8 + [ctypes.c_int] * 3 + [ctypes.c_void_p] + [ctypes.c_int] * 4)
+    L.irtt_last_error.restype = ctypes.c_char_p
+    L.irtt_attention_async.argtypes = L.irtt_attention.argtypes
+    dev = torch.device("cuda")
+    H, hd, S, C = 16, 128, 750, 576
+    D = H * hd
+    g = torch.Generator(device=dev).manual_seed(0)
+    mk = lambda n: torch.randn(n, D, device=dev, generator=g).to(torch.bfloat16)  # noqa: E731
+    q, k, v, ck_, cv = mk(2 * S), mk(2 * S), mk(2 * S), mk(C), mk(C)
+    gs = torch.sigmoid(torch.randn(2 * S, D, device=dev, generator=g)).to(torch.bfloat16)
+    out = torch.empty(2 * S, D, device=dev, dtype=torch.bfloat16)
+    seqs = [(0, S, 0, C), (S, S, 0, 0)]
+    sd = (ctypes.c_int * 8)(*[x for t in seqs for x in t])
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def launch():
+        rc = L.irtt_attention_async(P(q), P(k), P(v), P(gs), P(ck_), P(cv), None, sd, 2, H, hd, P(out), 1, 2 * S, C, 0)
+        if rc:
+            raise RuntimeError(L.irtt_last_error().decode())
+
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        launch()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    flops = 4 * S * (S + C) * D + 4 * S * S * D
+    return ms, flops / (ms / 1000.0) / 1e12
+
+
 def cpu_block_sample(target_s=12.0):
     """Times one DiT block (adaLN, joint attention over [latent | text | speaker]
     keys, SwiGLU) of the CPU oracle at the workload's median utterance size,
@@ -369,6 +410,8 @@ def main():
     ap.add_argument("--codec-only", action="store_true",
                     help="time the config-5 DACVAE decode alone (16 utterances, seeded latents)")
     ap.add_argument("--codec-precision", default="bf16", choices=["bf16", "f32"])
+    ap.add_argument("--attn-case", action="store_true",
+                    help="only the joint attention of one config-3 CFG layer, --steps launches (profiling case)")
     ap.add_argument("--ckpt", default=None)
     ap.add_argument("--latency-only", action="store_true",
                     help="only the config-3 single-utterance latency (used for profiling runs)")
@@ -381,6 +424,11 @@ def main():
         return latency_only(args)
     if args.codec_only:
         return codec_only(args)
+    if args.attn_case:
+        load_pkg()
+        ms, tf = attn_case(args.steps)
+        print(json.dumps({"attn_case_ms": round(ms, 4), "tflops": round(tf, 1)}), flush=True)
+        return 0
     if args.gemm_case:
         import torch
         load_pkg()

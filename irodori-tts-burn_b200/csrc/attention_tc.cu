@@ -156,11 +156,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         tma_load_2d(sV(s), m, V_FULL(s), h * HDIM, row_of(j));
         tma_load_2d(sV(s) + HALF, m, V_FULL(s), h * HDIM + 64, row_of(j));
       };
-      // K runs one tile ahead of V (K_j is consumed first and released earlier)
+      // K runs two tiles ahead of V, matching the MMA issue order
+      // S_0, S_1, then per j: S_{j+2}, P_j V_j
       if (ntiles > 0) load_k(0);
+      if (ntiles > 1) load_k(1);
       for (int j = 0; j < ntiles; ++j) {
-        if (j + 1 < ntiles) load_k(j + 1);
         load_v(j);
+        if (j + 2 < ntiles) load_k(j + 2);
       }
     }
   } else if (warp == 1) {
@@ -180,9 +182,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         umma_commit(S_FULL(s));
         umma_commit(K_EMPTY(s));
       };
+      // S_{j+2} goes out before P_j.V_j: its S buffer is free as soon as the
+      // group has loaded S_j into registers, so the next scores are computed
+      // while the group is still busy with the softmax of tile j.
       issue_s(0);
+      if (ntiles > 1) issue_s(1);
       for (int j = 0; j < ntiles; ++j) {
-        if (j + 1 < ntiles) issue_s(j + 1);
+        if (j + 2 < ntiles) issue_s(j + 2);
         const int s = j & 1;
         mbar_wait(V_FULL(s), (j >> 1) & 1);
         mbar_wait(P_FULL(s), (j >> 1) & 1);
@@ -279,6 +285,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive(P_FULL(b));
       last = j;
     }
+    // prefetch this row's gate half (independent of the attention result)
+    const int qi = q0 + row;
+    const long off = (long)(sd.tok_start + (qi < sd.len ? qi : 0)) * D + h * HDIM;
+    uint4 gpre[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      gpre[u] = (a.gsig && qi < sd.len) ? *reinterpret_cast<const uint4*>(a.gsig + off + grp * 64 + u * 8)
+                                        : make_uint4(0, 0, 0, 0);
     // this group's last P.V into O_grp
     if (last >= 0) mbar_wait(O_DONE(grp), (last >> 1) & 1);
     tc_fence_after();
@@ -300,10 +314,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     const float lsum = l0 * c0 + l1 * c1;
     const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
     const float w0 = c0 * inv, w1 = c1 * inv;
-    const int qi = q0 + row;
-    const long off = (long)(sd.tok_start + (qi < sd.len ? qi : 0)) * D + h * HDIM;
-#pragma unroll 1
-    for (int c = grp * 2; c < grp * 2 + 2; ++c) {
+#pragma unroll
+    for (int ci = 0; ci < 2; ++ci) {
+      const int c = grp * 2 + ci;
       uint32_t r0[32], r1[32];
       tmem_ld32(tmem + lane_off + TM_O + c * 32, r0);
       tmem_ld32(tmem + lane_off + TM_O + 128 + c * 32, r1);
@@ -313,7 +326,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int d0 = 0; d0 < 32; d0 += 8) {
           float g[8];
           if (a.gsig) {
-            const uint4 gv = *reinterpret_cast<const uint4*>(a.gsig + off + c * 32 + d0);
+            const uint4 gv = gpre[ci * 4 + d0 / 8];
             const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gv);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {

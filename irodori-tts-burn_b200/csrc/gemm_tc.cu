@@ -36,20 +36,27 @@ int read_and_clear_kernel_error() {
 
 namespace tc {
 
-constexpr int BM = 128, BK = 64, STAGES = 4, EPI_WARPS = 8, THREADS = 64 + 32 * EPI_WARPS;
+constexpr int BM = 128, BK = 64, EPI_WARPS = 8, THREADS = 64 + 32 * EPI_WARPS;
 constexpr uint32_t A_BYTES = BM * BK * 2;
 
-template <int BN>
+// CG = CTAs per MMA: 1, or 2 for a CTA pair (cluster of 2) that computes a
+// 256-row tile with tcgen05.mma.cta_group::2.  In a pair each CTA stages its
+// own 128 rows of A and one half (BN/2 rows) of B; the MMA reads both halves,
+// so every SM streams one third less operand data through shared memory per
+// FLOP than a 1-CTA 128 x BN tile.
+template <int BN, int CG>
 struct Cfg {
-  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr int B_ROWS = BN / CG;  // B rows staged by each CTA
+  static constexpr uint32_t B_BYTES = B_ROWS * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
   // stages | barriers (256 B) | one 32x33 f32 transpose buffer per epilogue warp | alignment slack
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 256 + EPI_WARPS * 32 * 33 * 4 + 1024;
   // instruction descriptor, kind::f16: D=f32 (bit4), A=B=bf16 (bits 7,10), K-major
-  // both, N>>3 at bits 17-22, M>>4 at bits 24-28.
+  // both, N>>3 at bits 17-22, M>>4 at bits 24-28 (M = 128 per CTA of the group).
   static constexpr uint32_t IDESC =
-      (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+      (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)((BM * CG) >> 4) << 24);
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -125,6 +132,52 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
+// CTA-pair forms (cta_group::2).  The MMA and its commits are issued by the
+// pair's rank-0 CTA; a commit with .multicast::cluster arrives on the barrier
+// at the same shared-memory offset in every CTA of the mask.
+__device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                              uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+// Address of the same shared-memory location in the pair's rank-0 CTA.
+__device__ __forceinline__ uint32_t map_rank0(uint32_t saddr) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(saddr));
+  return r;
+}
+// 2-D TMA load into this CTA's shared memory whose completion is counted on
+// an mbarrier of the pair's rank-0 CTA (no multicast).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_rank0, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_rank0), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -163,13 +216,17 @@ struct Regs {
   __device__ __forceinline__ float operator()(int j) const { return __uint_as_float(r[j]); }
 };
 
-template <int BN>
 // 320 threads: registers are budgeted per 4-warp group, so 10 warps cost as
 // much as 12 and the kernel must stay at or below 168 registers per thread.
+// CG = 2: launched as clusters of 2 CTAs (consecutive blockIdx.x); the pair
+// walks the same work units, rank 0 issues the MMAs for both.
+template <int BN, int CG>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
                 int splits, const __grid_constant__ EpiParams ep) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, CG>;
+  constexpr int STAGES = C::STAGES;
+  constexpr int BMT = BM * CG;  // rows of one work tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
@@ -178,7 +235,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
+  const uint32_t rank = CG == 2 ? cluster_rank() : 0u;
+  const int grp0 = blockIdx.x / CG, ngrp = gridDim.x / CG;  // work-group index and count
+  const int m_tiles = (M + BMT - 1) / BMT, n_tiles = (N + BN - 1) / BN;
   const int num_tiles = m_tiles * n_tiles;
   const int k_blocks = (K + BK - 1) / BK;
   // work unit = (tile, K-split); splits > 1 only for the additive RESID epilogue
@@ -197,19 +256,29 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull(b), 1);
-      mbar_init(tempty(b), EPI_WARPS);
+      // rank 0's accumulator-empty barrier counts the epilogue warps of the group
+      mbar_init(tempty(b), EPI_WARPS * CG);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(C::TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (CG == 2) {
+      // executed by one warp in each CTA of the pair: same columns in both
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(C::TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(C::TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // the peer signals rank 0's barriers: both CTAs' barriers exist from here on
+  if constexpr (CG == 2) cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // the prologue above may overlap the previous kernel; operands are read only now
@@ -220,29 +289,38 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       uint32_t it = 0;
-      for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+      for (int u = grp0; u < num_units; u += ngrp) {
         const int t = u / splits, sp = u - t * splits;
         const int kb0 = sp * kpb, kb1 = min(k_blocks, kb0 + kpb);
         int mi_, ni_;
         tile_coords(t, m_tiles, n_tiles, mi_, ni_);
-        const int m0 = mi_ * BM, n0 = ni_ * BN;
+        const int m0 = mi_ * BMT + (int)rank * BM, n0 = ni_ * BN + (int)rank * C::B_ROWS;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           mbar_wait(empty(s), ph ^ 1);
           uint8_t* a_dst = tiles + s * C::STAGE_BYTES;
           uint8_t* b_dst = a_dst + A_BYTES;
-          mbar_expect_tx(full(s), C::STAGE_BYTES);
-          tma_load_2d(smem_u32(a_dst), &tmA, full(s), kb * BK, m0);
-          tma_load_2d(smem_u32(b_dst), &tmB, full(s), kb * BK, n0);
+          if constexpr (CG == 2) {
+            // both CTAs' copies complete on rank 0's full barrier, which
+            // expects the pair's bytes
+            const uint32_t fb = map_rank0(full(s));
+            if (rank == 0) mbar_expect_tx(full(s), CG * C::STAGE_BYTES);
+            tma_load_2d_pair(smem_u32(a_dst), &tmA, fb, kb * BK, m0);
+            tma_load_2d_pair(smem_u32(b_dst), &tmB, fb, kb * BK, n0);
+          } else {
+            mbar_expect_tx(full(s), C::STAGE_BYTES);
+            tma_load_2d(smem_u32(a_dst), &tmA, full(s), kb * BK, m0);
+            tma_load_2d(smem_u32(b_dst), &tmB, full(s), kb * BK, n0);
+          }
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer (rank 0 of a pair) ----------------
+    if (lane == 0 && rank == 0) {
       uint32_t it = 0, tl = 0;
-      for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++tl) {
+      for (int u = grp0; u < num_units; u += ngrp, ++tl) {
         const int t = u / splits, sp = u - t * splits;
         const int kb0 = sp * kpb, kb1 = min(k_blocks, kb0 + kpb);
         const int buf = tl & 1;
@@ -259,12 +337,20 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            umma_f16(d_tmem, sdesc(a_addr + kk * 32), sdesc(b_addr + kk * 32), C::IDESC,
-                     (kb != kb0 || kk != 0) ? 1u : 0u);
+            if constexpr (CG == 2)
+              umma_f16_pair(d_tmem, sdesc(a_addr + kk * 32), sdesc(b_addr + kk * 32), C::IDESC,
+                            (kb != kb0 || kk != 0) ? 1u : 0u);
+            else
+              umma_f16(d_tmem, sdesc(a_addr + kk * 32), sdesc(b_addr + kk * 32), C::IDESC,
+                       (kb != kb0 || kk != 0) ? 1u : 0u);
           }
-          umma_commit(empty(s));  // frees the smem stage when these MMAs complete
+          // frees the smem stage (in both CTAs of a pair) when these MMAs complete
+          if constexpr (CG == 2) umma_commit_pair(empty(s));
+          else umma_commit(empty(s));
         }
-        umma_commit(tfull(buf));  // accumulator ready
+        // accumulator ready (both CTAs' epilogues)
+        if constexpr (CG == 2) umma_commit_pair(tfull(buf));
+        else umma_commit(tfull(buf));
       }
     }
   } else {
@@ -272,13 +358,16 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int quad = warp & 3;       // TMEM lane quadrant this warp may access
     const int half = (warp - 2) / 4;  // which columns of the tile it takes
     uint32_t tl = 0;
-    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++tl) {
+    // rank 0's accumulator-empty barriers, addressed through the cluster window
+    const uint32_t te0 = CG == 2 ? map_rank0(tempty(0)) : tempty(0);
+    const uint32_t te1 = CG == 2 ? map_rank0(tempty(1)) : tempty(1);
+    for (int u = grp0; u < num_units; u += ngrp, ++tl) {
       const int t = u / splits;
       const int buf = tl & 1;
       const uint32_t aph = (tl >> 1) & 1;
       int mi_, ni_;
       tile_coords(t, m_tiles, n_tiles, mi_, ni_);
-      const int m0 = mi_ * BM, n0 = ni_ * BN;
+      const int m0 = mi_ * BMT + (int)rank * BM, n0 = ni_ * BN;
       mbar_wait(tfull(buf), aph);
       tc_fence_after();
       const int row = m0 + quad * 32 + lane;
@@ -361,14 +450,22 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(tempty(buf));
+      if (lane == 0) {
+        if constexpr (CG == 2) mbar_arrive_cluster(buf ? te1 : te0);
+        else mbar_arrive(tempty(buf));
+      }
     }
   }
 
   __syncthreads();
+  // a pair stays resident until neither CTA signals the other any more
+  if constexpr (CG == 2) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS));
+    if constexpr (CG == 2)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS));
   }
 }
 
@@ -440,23 +537,81 @@ int num_sms() {
   return n;
 }
 
+// Co-resident CTA pairs of gemm_kernel<BN, 2> on this device (cached).
 template <int BN>
+int max_pairs() {
+  static int cached[32] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& n = cached[dev & 31];
+  if (!n) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 1024);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = Cfg<BN, 2>::SMEM;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int c = 0;
+    if (cudaOccupancyMaxActiveClusters(&c, gemm_kernel<BN, 2>, &cfg) != cudaSuccess || c <= 0) {
+      cudaGetLastError();
+      c = num_sms() / 2;
+    }
+    n = c;
+  }
+  return n;
+}
+
+template <int BN, int CG>
 void launch(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int K, int splits, const EpiParams& p,
             cudaStream_t s) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, CG>;
   static unsigned attr_mask = 0;  // per-device opt-in to the large dynamic smem
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_mask & (1u << (dev & 31)))) {
-    IRT_CUDA(cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
+    IRT_CUDA(cudaFuncSetAttribute(gemm_kernel<BN, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
     attr_mask |= 1u << (dev & 31);
   }
   const CUtensorMap ta = tensor_map(A, M, K, lda, BM);  // copies: the cache may be cleared
-  const CUtensorMap tb = tensor_map(B, N, K, ldb, BN);
-  int units = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * splits;
-  int grid = units < num_sms() ? units : num_sms();
-  launch_pdl(gemm_kernel<BN>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, M, N, K, splits, p);
+  const CUtensorMap tb = tensor_map(B, N, K, ldb, C::B_ROWS);
+  const int units = ((M + BM * CG - 1) / (BM * CG)) * ((N + BN - 1) / BN) * splits;
+  if constexpr (CG == 1) {
+    const int grid = units < num_sms() ? units : num_sms();
+    launch_pdl(gemm_kernel<BN, 1>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, M, N, K, splits, p);
+  } else {
+    const int pairs = std::min(units, max_pairs<BN>());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    IRT_CUDA(cudaLaunchKernelEx(&cfg, gemm_kernel<BN, 2>, ta, tb, M, N, K, splits, p));
+  }
   IRT_CHECK_LAUNCH();
+}
+
+// CTA pairs (cta_group::2) for every GEMM with at least two 128-row tiles,
+// unless IRT_GEMM_PAIRS=0.
+bool use_pairs(int M) {
+  static const bool on = [] {
+    const char* e = std::getenv("IRT_GEMM_PAIRS");
+    return !(e && e[0] == '0');
+  }();
+  return on && M >= 2 * BM;
 }
 
 // Fraction of the SM-slots of the last wave that do useful work.
@@ -484,8 +639,11 @@ bool gemm_tc_supported(const EpiParams& p, int K, long lda, long ldb, const void
 void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int K, const EpiParams& p,
              cudaStream_t s) {
   // Tile width: 256 unless 128 fills the last wave clearly better (small M).
-  const int sms = tc::num_sms();
-  const long mt = (M + tc::BM - 1) / tc::BM;
+  // Work slots are SMs (1-CTA tiles of 128 rows) or SM pairs (256 rows).
+  const bool pairs = tc::use_pairs(M);
+  const int sms = pairs ? tc::num_sms() / 2 : tc::num_sms();
+  const int bmt = pairs ? 2 * tc::BM : tc::BM;
+  const long mt = (M + bmt - 1) / bmt;
   const long t256 = mt * ((N + 255) / 256), t128 = mt * ((N + 127) / 128);
   bool use256 = N >= 256;
   if ((p.mode == EPI_QKVG || p.mode == EPI_CTXKV) && (p.Dq % 256)) use256 = false;
@@ -501,8 +659,13 @@ void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int
     const int kpb = (kb + splits - 1) / splits;
     splits = (kb + kpb - 1) / kpb;  // no empty split
   }
-  if (use256) tc::launch<256>(A, lda, B, ldb, M, N, K, splits, p, s);
-  else tc::launch<128>(A, lda, B, ldb, M, N, K, splits, p, s);
+  if (pairs) {
+    if (use256) tc::launch<256, 2>(A, lda, B, ldb, M, N, K, splits, p, s);
+    else tc::launch<128, 2>(A, lda, B, ldb, M, N, K, splits, p, s);
+  } else {
+    if (use256) tc::launch<256, 1>(A, lda, B, ldb, M, N, K, splits, p, s);
+    else tc::launch<128, 1>(A, lda, B, ldb, M, N, K, splits, p, s);
+  }
 }
 
 }  // namespace irt

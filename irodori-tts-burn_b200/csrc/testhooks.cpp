@@ -114,6 +114,37 @@ IRTT_API int irtt_attention(const void* q, const void* k, const void* v, const v
   });
 }
 
+// Same as irtt_attention without the synchronisation (profiling loops): the
+// sequence table is uploaded once per distinct table and kept; check the
+// watchdog with irtt_sync_check() afterwards.
+IRTT_API int irtt_attention_async(const void* q, const void* k, const void* v, const void* g, const void* ck,
+                                  const void* cv, const uint8_t* key_mask, const int* seqs_host, int nseq, int H,
+                                  int hd, void* out, int bf16_io, int rows, int ctx_rows, int path) {
+  return guard([&] {
+    static irt::DevBuf d;
+    static std::vector<int> cached;
+    std::vector<int> tab(seqs_host, seqs_host + 4 * nseq);
+    int mx = 0;
+    for (int i = 0; i < nseq; ++i) mx = std::max(mx, seqs_host[4 * i + 1]);
+    if (tab != cached) {
+      d.ensure(sizeof(irt::SeqDesc) * std::max(1, nseq));
+      IRT_CUDA(cudaMemcpy(d.p, tab.data(), sizeof(int) * tab.size(), cudaMemcpyHostToDevice));
+      cached = tab;
+    }
+    irt::AttnParams p{};
+    p.q = q; p.k = k; p.v = v; p.gsig = g; p.ck = ck; p.cv = cv; p.key_mask = key_mask;
+    p.seqs = d.as<irt::SeqDesc>();
+    p.nseq = nseq; p.max_len = mx; p.H = H; p.hd = hd;
+    p.scale = 1.0f / sqrtf((float)hd);
+    p.out = out;
+    p.rows = rows;
+    p.ctx_rows = ctx_rows;
+    p.path = path;
+    if (path == 0 && bf16_io && !irt::attention_tc_supported(p)) throw irt::Error(4, "tcgen05 attention unsupported");
+    irt::attention(p, bf16_io, nullptr);
+  });
+}
+
 IRTT_API long long irtt_launch_count() { return irt::launch_counter().load(); }
 
 // Synchronise the device and report the GEMM pipeline watchdog flag.
