@@ -212,6 +212,7 @@ IRT_API int irt_codec_decode_ragged(irt_codec* c, const float* latent, int32_t b
  * whose own allocator already holds the free HBM.  All intermediate
  * activations live in one 16 MiB device array compiled into the library (held
  * by every GPU that loads it until exit), so the call allocates nothing.
+ * It always runs the fp32 SIMT decoder, whatever the codec's precision.
  *   - latent [batch, frames, 32] and wav [batch, 1, frames * hop] must be
  *     device (or managed) memory; the call returns once wav is complete.
  *   - Capacity: batch * frames <= 7 latent frames (280 ms) for the full-width

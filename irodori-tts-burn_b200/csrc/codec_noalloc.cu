@@ -4,10 +4,11 @@
 // e.g. a real-time streaming loop that decodes short latent chunks and cannot
 // afford the implicit device-wide synchronisation of cudaMalloc / cudaFree, or
 // a host application whose framework allocator has already reserved the free
-// HBM so that a fresh cudaMalloc would fail.  This path decodes with the same
-// kernels as irt_codec_decode but keeps every intermediate activation in one
-// fixed device array compiled into the library, so a call performs no
-// cudaMalloc, cudaFree or allocating library call.
+// HBM so that a fresh cudaMalloc would fail.  This path decodes with the fp32
+// SIMT kernels of irt_codec_decode's f32 mode (whatever the codec's
+// precision) but keeps every intermediate activation in one fixed device
+// array compiled into the library, so a call performs no cudaMalloc, cudaFree
+// or allocating library call.
 //
 // Limits and sharing rules:
 //  - The scratch array holds CODEC_NOALLOC_SCRATCH_FLOATS floats (16 MiB).
