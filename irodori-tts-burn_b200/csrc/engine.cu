@@ -433,7 +433,7 @@ void Engine::forward_step(int M, const SeqDesc* d_seqs, int nseq, int max_len, i
   ada_cur.ensure(ada_bytes);
   IRT_CUDA(cudaMemcpyAsync(ada_cur.p, ws.ada.as<uint8_t>() + (size_t)t_index * ada_bytes, ada_bytes,
                            cudaMemcpyDeviceToDevice, s));
-  if (!use_graphs) {
+  if (!use_graphs || dump_layers) {
     dit_forward(M, d_seqs, nseq, max_len, ada_cur.as<float>(), nrows_ctx, s);
     return;
   }
@@ -489,6 +489,13 @@ void Engine::dit_forward(int M, const SeqDesc* d_seqs, int nseq, int max_len, co
     p.bias = in_b.as<float>();
     gemm(ws.xin.p, P, in_w, M, D, P, p, s);
   }
+  float* dump = dump_layers;
+  if (dump) {
+    if (M > dump_rows_cap) throw shape_error("layer dump buffer too small");
+    dump_rows = M;
+    dump_layers = nullptr;  // first forward only
+    IRT_CUDA(cudaMemcpyAsync(dump, x, (size_t)M * D * 4, cudaMemcpyDeviceToDevice, s));
+  }
   for (int l = 0; l < L; ++l) {
     const float* ad = ada_t + (size_t)l * 6 * D;
     auto& b = blk[l];
@@ -532,6 +539,9 @@ void Engine::dit_forward(int M, const SeqDesc* d_seqs, int nseq, int max_len, co
     r2.x = x;
     r2.gate = ad + 5 * D;
     gemm(ws.hm.p, F, b.w2, M, D, F, r2, s);
+    if (dump)
+      IRT_CUDA(cudaMemcpyAsync(dump + (size_t)(l + 1) * dump_rows_cap * D, x, (size_t)M * D * 4,
+                               cudaMemcpyDeviceToDevice, s));
   }
   // out_norm + out_proj fused (narrow N = P): one pass over x per row
   rmsnorm_proj(x, out_norm.as<float>(), out_w.p, bf, out_b.as<float>(), ws.vout.as<float>(), M, D, P, eps, s);

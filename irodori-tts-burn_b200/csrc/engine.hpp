@@ -76,6 +76,14 @@ struct Engine {
   // address it bakes in.  A key's first use runs eagerly (so workspaces are
   // allocated outside capture); its second use captures and instantiates.
   bool use_graphs = true;
+  // Per-layer capture for parity tests (test hooks only): when set, the next
+  // DiT forward runs eagerly and copies the f32 residual stream after in_proj
+  // and after every block into dump_layers[(0..L) * M * D] (device memory with
+  // room for dump_rows_cap rows per slot), records the row count in dump_rows,
+  // and then clears the pointer.
+  float* dump_layers = nullptr;
+  int dump_rows_cap = 0;
+  int dump_rows = 0;
   std::map<std::vector<uintptr_t>, cudaGraphExec_t> graphs;
   std::map<std::vector<uintptr_t>, int> graph_seen;
   std::map<std::vector<uintptr_t>, long long> graph_kernels;

@@ -6,6 +6,7 @@
 
 #include "codec.hpp"
 #include "common.hpp"
+#include "engine.hpp"
 #include "kernels.hpp"
 
 #define IRTT_API extern "C" __attribute__((visibility("default")))
@@ -184,5 +185,24 @@ IRTT_API int irtt_conv_tc(const void* in, int rows_in, int cin, const void* w, i
     irt::conv_tc(reinterpret_cast<const irt::bf16*>(in), reinterpret_cast<const irt::bf16*>(w), a, nullptr);
     IRT_CUDA(cudaDeviceSynchronize());
     if (irt::conv_tc_read_and_clear_error()) throw irt::Error(20, "conv_tc watchdog fired");
+  });
+}
+
+// Runs one sample() of a fresh engine and captures the f32 residual stream of
+// its first DiT forward: after in_proj and after each of the L blocks, for all
+// packed rows (CFG groups x utterance frames).  dump: device [(L + 1) * cap * D].
+// Returns the captured row count in *rows.  The latent output goes to out_host.
+IRTT_API int irtt_sample_dump_layers(const char* ckpt, int precision, const irt_sampler_params* sp,
+                                     const irt_request* rq, float* out_host, float* dump, int cap, int* rows) {
+  return guard([&] {
+    irt::Engine e(0, ckpt, precision);
+    irt::validate_sampler_params(*sp);
+    e.params = *sp;
+    e.has_params = true;
+    e.dump_layers = dump;
+    e.dump_rows_cap = cap;
+    e.sample(*rq, out_host, IRT_MEM_HOST, nullptr);
+    IRT_CUDA(cudaDeviceSynchronize());
+    *rows = e.dump_rows;
   });
 }
