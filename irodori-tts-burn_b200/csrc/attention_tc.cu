@@ -229,13 +229,22 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(S_EMPTY(b));  // S buffer may be overwritten now
-      float mx = -INFINITY;
+      // Row max on the raw scores (the softmax scale is positive); keys past
+      // the sequence end (only in a ragged last tile) become -inf.
+      if (kvalid < KT) {
 #pragma unroll
-      for (int i = 0; i < KT; ++i) {
-        const float v = i < kvalid ? __uint_as_float(sr[i]) * a.scale_log2 : -INFINITY;
-        sr[i] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
+        for (int i = 0; i < KT; ++i)
+          if (i >= kvalid) sr[i] = __float_as_uint(-INFINITY);
       }
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < KT; i += 4) {
+        mx0 = fmaxf(mx0, __uint_as_float(sr[i]));
+        mx1 = fmaxf(mx1, __uint_as_float(sr[i + 1]));
+        mx2 = fmaxf(mx2, __uint_as_float(sr[i + 2]));
+        mx3 = fmaxf(mx3, __uint_as_float(sr[i + 3]));
+      }
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.scale_log2;  // log2 domain
       // conditional rescale of the running max
       float corr = 1.f;
       bool raise = mx > m_run + RESCALE_LOG2 || (m_run == -INFINITY && mx > -INFINITY);
@@ -243,7 +252,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         corr = m_run == -INFINITY ? 0.f : ex2(m_run - mx);
         m_run = mx;
       }
-      const float base = m_run == -INFINITY ? 0.f : m_run;
+      // p = 2^(s * scale - m): one FFMA feeds the exponential
+      const float nbase = m_run == -INFINITY ? 0.f : -m_run;
       // P = exp2(s - m) -> bf16 swizzled tile; row sum in f32
       mbar_wait(P_EMPTY(b), ((j >> 1) & 1) ^ 1);
       float rsum = 0.f;
@@ -254,8 +264,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int i = chunk * 8 + 2 * q;
-          const float p0 = ex2(__uint_as_float(sr[i]) - base);
-          const float p1 = ex2(__uint_as_float(sr[i + 1]) - base);
+          const float p0 = ex2(fmaf(__uint_as_float(sr[i]), a.scale_log2, nbase));
+          const float p1 = ex2(fmaf(__uint_as_float(sr[i + 1]), a.scale_log2, nbase));
           rsum += p0 + p1;
           __nv_bfloat162 t = __floats2bfloat162_rn(p0, p1);
           pk[q] = *reinterpret_cast<uint32_t*>(&t);
