@@ -1,26 +1,31 @@
 // tcgen05 / TMEM flash attention for sm_100a (hd = 128, bf16 operands).
 //
 // One CTA = one (sequence, head, 128-query tile).  320 threads:
-//   warp 0      TMA producer: Q once; per 128-key tile a K tile and a V tile,
-//               each on its own 2-stage ring (self keys first, then context)
-//   warp 1      TMEM allocator + single-thread MMA issuer:
-//                 S_j  = Q K_j^T       (M=128 queries, N=128 keys, K=128 hd) -> TMEM S[j&1]
-//                 O_b += P_j V_j, b = j&1  (M=128, N=128 hd, K=128 keys; V MN-major)
-//   warps 2..9  two softmax warpgroups; group b takes key tiles j = b, b+2, ...
-//               with its own running max / sum and its own TMEM accumulator
-//               O_b, so the two groups' exponentials run concurrently.  Thread
-//               r of a group owns query row r.  Per tile it loads the S row
-//               from TMEM (one batched wait), masks, takes the row max, writes
-//               P = exp2(s - m) as bf16 (128B-swizzled, K-major) to shared
-//               memory and keeps the row sum.  The running max is only raised
-//               when a row max grows by more than 2^8 (conditional rescale);
-//               then the warp rescales its O_b rows in TMEM after the previous
-//               P.V into O_b has completed.  Skipping is exact: O_b and l_b
-//               share the same stale max.  At the end the groups exchange
-//               (m, l) through shared memory and each merges one 64-column
-//               half: O = (O_0 2^(m_0-m) + O_1 2^(m_1-m)) / (l_0 2^(m_0-m) + l_1 2^(m_1-m)).
+//   warp 0      TMA producer: per 128-key tile a K tile and a V tile, each on
+//               its own 2-stage ring (self keys first, then context); K runs
+//               two tiles ahead of V
+//   warp 1      TMEM allocator + single-thread MMA issuer, both products with
+//               the A operand in tensor memory so only K and V are read from
+//               shared memory:
+//                 S_j  = Q K_j^T   (A = Q in TMEM, B = K_j K-major)  -> TMEM S[j&1]
+//                 O   += P_j V_j   (A = P_j in TMEM, B = V_j MN-major) -> TMEM O
+//               issue order S_0, S_1, then per j: P_j V_j, S_{j+2}; S_{j+2}
+//               overwrites the buffer that held S_j / P_j, which the in-order
+//               tensor pipe has consumed by then
+//   warps 2..9  softmax: thread r of a warp owns query row r of its TMEM lane
+//               quadrant; the two warps of a quadrant split the 128 keys of a
+//               tile (64 each) and exchange row maxima through shared memory.
+//               Per tile a warp loads its 64 scores (one batched wait), takes
+//               the row max on raw scores, writes P = exp2(s*scale - m) as
+//               packed bf16 over its scores' columns (the A operand of P V),
+//               and keeps its half of the row sum.  The running max is only
+//               raised when a row max grows by more than 2^8 (conditional
+//               rescale); then each warp rescales its 64 O columns after the
+//               previous P V has completed.  Skipping is exact: O and l share
+//               the same stale max.
+// TMEM columns: S0 [0,128) S1 [128,256) O [256,384) Q [384,448).
 // Keys past a sequence's end get -inf scores; a row with no valid key outputs
-// 0.  Output = O * sigmoid-gate, bf16.
+// 0.  Output = (O / l) * sigmoid-gate, bf16.
 #include <algorithm>
 
 #include "common.hpp"
@@ -35,25 +40,23 @@ namespace {
 
 using namespace tcx;
 
-constexpr int QT = 128, KT = 128, HDIM = 128, THREADS = 320;
-constexpr uint32_t TILE_BYTES = QT * HDIM * 2;  // 32 KB (two 16 KB 64-column halves)
+constexpr int QT = 128, KT = 128, HDIM = 128, THREADS = 320, NKV = 2;
+constexpr uint32_t TILE_BYTES = KT * HDIM * 2;  // 32 KB (two 16 KB 64-column halves)
 constexpr uint32_t HALF = TILE_BYTES / 2;
-// smem: Q | K0 K1 | V0 V1 | P0 P1 | barriers
-constexpr uint32_t OFF_Q = 0, OFF_K = TILE_BYTES, OFF_V = OFF_K + 2 * TILE_BYTES, OFF_P = OFF_V + 2 * TILE_BYTES;
-constexpr uint32_t OFF_BAR = OFF_P + 2 * TILE_BYTES;
+// smem: K ring | V ring | exchange | barriers
+constexpr uint32_t OFF_K = 0, OFF_V = NKV * TILE_BYTES;
+constexpr uint32_t OFF_X = OFF_V + NKV * TILE_BYTES;  // [2 slots][2 halves][128 rows] f32 maxima, [2][128] sums
+constexpr uint32_t X_BYTES = (2 * 2 * 128 + 2 * 128) * 4;
+constexpr uint32_t OFF_BAR = OFF_X + X_BYTES;
 constexpr size_t SMEM = OFF_BAR + 256 + 1024;
-// (m, l) exchange of the final merge, [2 groups][m, l][128 rows] f32, in the Q
-// tile: once every group has seen its last P.V complete, every QK^T MMA
-// (issued before those P.V, and tracked by their commits) has finished
-// reading Q.
-constexpr uint32_t OFF_XCHG = OFF_Q;
 constexpr uint32_t IDESC_S = idesc_bf16(128, 128, false);
 constexpr uint32_t IDESC_O = idesc_bf16(128, 128, true);
-constexpr uint32_t TM_S = 0, TM_O = 256;  // TMEM columns: S double buffer, O_0 | O_1 accumulators
-constexpr float RESCALE_LOG2 = 8.f;       // raise the running max only beyond 2^8 growth
+constexpr uint32_t TM_S = 0, TM_O = 256, TM_Q = 384;
+constexpr float RESCALE_LOG2 = 8.f;  // raise the running max only beyond 2^8 growth
 
 struct TcAttnArgs {
   const SeqDesc* seqs;
+  const bf16* q;
   const bf16* gsig;
   bf16* out;
   int H;
@@ -73,10 +76,25 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// tcgen05.mma with the A operand in tensor memory (K-major, two bf16 per
+// 32-bit column: element k of a row sits in column k / 2).
+__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&t);
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmCK,
-                   const __grid_constant__ CUtensorMap tmCV, const __grid_constant__ TcAttnArgs a) {
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                   const __grid_constant__ CUtensorMap tmCK, const __grid_constant__ CUtensorMap tmCV,
+                   const __grid_constant__ TcAttnArgs a) {
   pdl_wait();  // before any read of predecessor output, in every CTA
   pdl_trigger();
   const SeqDesc sd = a.seqs[blockIdx.z];
@@ -88,17 +106,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  const uint32_t Q_FULL = bar(0);
-  auto O_DONE = [&](int b) { return bar(18 + b); };
+  const uint32_t Q_READY = bar(0), O_DONE = bar(1);
   auto K_FULL = [&](int s) { return bar(2 + s); };
-  auto K_EMPTY = [&](int s) { return bar(4 + s); };
-  auto V_FULL = [&](int s) { return bar(6 + s); };
-  auto V_EMPTY = [&](int s) { return bar(8 + s); };
-  auto S_FULL = [&](int b) { return bar(10 + b); };
-  auto S_EMPTY = [&](int b) { return bar(12 + b); };
-  auto P_FULL = [&](int b) { return bar(14 + b); };
-  auto P_EMPTY = [&](int b) { return bar(16 + b); };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  auto K_EMPTY = [&](int s) { return bar(2 + NKV + s); };
+  auto V_FULL = [&](int s) { return bar(2 + 2 * NKV + s); };
+  auto V_EMPTY = [&](int s) { return bar(2 + 3 * NKV + s); };
+  auto S_FULL = [&](int b) { return bar(2 + 4 * NKV + b); };
+  auto P_FULL = [&](int b) { return bar(4 + 4 * NKV + b); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6 + 4 * NKV);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_self = (sd.len + KT - 1) / KT;
@@ -106,17 +121,17 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int ntiles = n_self + n_ctx;
 
   if (threadIdx.x == 0) {
-    mbar_init(Q_FULL, 1);
+    mbar_init(Q_READY, 8);
+    mbar_init(O_DONE, 1);
+    for (int r = 0; r < NKV; ++r) {
+      mbar_init(K_FULL(r), 1);
+      mbar_init(K_EMPTY(r), 1);
+      mbar_init(V_FULL(r), 1);
+      mbar_init(V_EMPTY(r), 1);
+    }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(O_DONE(b), 1);
-      mbar_init(K_FULL(b), 1);
-      mbar_init(K_EMPTY(b), 1);
-      mbar_init(V_FULL(b), 1);
-      mbar_init(V_EMPTY(b), 1);
       mbar_init(S_FULL(b), 1);
-      mbar_init(S_EMPTY(b), 4);
-      mbar_init(P_FULL(b), 4);
-      mbar_init(P_EMPTY(b), 1);
+      mbar_init(P_FULL(b), 8);
     }
     mbar_fence_init();
   }
@@ -125,39 +140,32 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t sQ = smem_u32(sm + OFF_Q);
   auto sK = [&](int s) { return smem_u32(sm + OFF_K + s * TILE_BYTES); };
   auto sV = [&](int s) { return smem_u32(sm + OFF_V + s * TILE_BYTES); };
-  auto sP = [&](int b) { return smem_u32(sm + OFF_P + b * TILE_BYTES); };
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      prefetch_map(&tmQ);
       prefetch_map(&tmK);
       prefetch_map(&tmV);
-      mbar_expect_tx(Q_FULL, TILE_BYTES);
-      tma_load_2d(sQ, &tmQ, Q_FULL, h * HDIM, sd.tok_start + q0);
-      tma_load_2d(sQ + HALF, &tmQ, Q_FULL, h * HDIM + 64, sd.tok_start + q0);
       auto row_of = [&](int j) { return j < n_self ? sd.tok_start + j * KT : sd.ctx_off + (j - n_self) * KT; };
       auto load_k = [&](int j) {
-        const int s = j & 1;
-        mbar_wait(K_EMPTY(s), ((j >> 1) & 1) ^ 1);
+        const int s = j % NKV;
+        mbar_wait(K_EMPTY(s), ((j / NKV) & 1) ^ 1);
         mbar_expect_tx(K_FULL(s), TILE_BYTES);
         const CUtensorMap* m = j < n_self ? &tmK : &tmCK;
         tma_load_2d(sK(s), m, K_FULL(s), h * HDIM, row_of(j));
         tma_load_2d(sK(s) + HALF, m, K_FULL(s), h * HDIM + 64, row_of(j));
       };
       auto load_v = [&](int j) {
-        const int s = j & 1;
-        mbar_wait(V_EMPTY(s), ((j >> 1) & 1) ^ 1);
+        const int s = j % NKV;
+        mbar_wait(V_EMPTY(s), ((j / NKV) & 1) ^ 1);
         mbar_expect_tx(V_FULL(s), TILE_BYTES);
         const CUtensorMap* m = j < n_self ? &tmV : &tmCV;
         tma_load_2d(sV(s), m, V_FULL(s), h * HDIM, row_of(j));
         tma_load_2d(sV(s) + HALF, m, V_FULL(s), h * HDIM + 64, row_of(j));
       };
-      // K runs two tiles ahead of V, matching the MMA issue order
-      // S_0, S_1, then per j: S_{j+2}, P_j V_j
+      // K two tiles ahead of V, matching the MMA issue order
       if (ntiles > 0) load_k(0);
       if (ntiles > 1) load_k(1);
       for (int j = 0; j < ntiles; ++j) {
@@ -168,201 +176,179 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0 && ntiles > 0) {
-      mbar_wait(Q_FULL, 0);
+      mbar_wait(Q_READY, 0);
+      tc_fence_after();
       auto issue_s = [&](int j) {
-        const int s = j & 1;
-        mbar_wait(K_FULL(s), (j >> 1) & 1);
-        mbar_wait(S_EMPTY(s), ((j >> 1) & 1) ^ 1);
+        const int r = j % NKV, b = j & 1;
+        mbar_wait(K_FULL(r), (j / NKV) & 1);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HDIM / 16; ++kk) {
           const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-          umma_f16(tmem + TM_S + s * 128, sdesc_kmajor(sQ + off), sdesc_kmajor(sK(s) + off), IDESC_S, kk != 0);
+          umma_ts(tmem + TM_S + b * 128, tmem + TM_Q + kk * 8, sdesc_kmajor(sK(r) + off), IDESC_S, kk != 0);
         }
-        umma_commit(S_FULL(s));
-        umma_commit(K_EMPTY(s));
+        umma_commit(S_FULL(b));
+        umma_commit(K_EMPTY(r));
       };
-      // S_{j+2} goes out before P_j.V_j: its S buffer is free as soon as the
-      // group has loaded S_j into registers, so the next scores are computed
-      // while the group is still busy with the softmax of tile j.
       issue_s(0);
       if (ntiles > 1) issue_s(1);
       for (int j = 0; j < ntiles; ++j) {
-        if (j + 2 < ntiles) issue_s(j + 2);
-        const int s = j & 1;
-        mbar_wait(V_FULL(s), (j >> 1) & 1);
+        const int s = j & 1, r = j % NKV;
+        mbar_wait(V_FULL(r), (j / NKV) & 1);
         mbar_wait(P_FULL(s), (j >> 1) & 1);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < KT / 16; ++kk) {
-          // A = P (K-major over keys); B = V [keys][hd] (MN-major: 64-column
-          // halves 16 KB apart, 8-key groups 1 KB apart)
-          const uint32_t aoff = (kk >> 2) * HALF + (kk & 3) * 32;
-          const uint64_t bdesc = sdesc_sw128(sV(s) + kk * 16 * 128, HALF, 1024);
-          umma_f16(tmem + TM_O + s * 128, sdesc_kmajor(sP(s) + aoff), bdesc, IDESC_O, (j >= 2 || kk != 0));
+          // A = P_j (keys 16kk..16kk+15 packed in 8 columns of S buffer s);
+          // B = V [keys][hd] (MN-major: 64-column halves 16 KB apart, 8-key
+          // groups 1 KB apart)
+          const uint64_t bdesc = sdesc_sw128(sV(r) + kk * 16 * 128, HALF, 1024);
+          umma_ts(tmem + TM_O, tmem + TM_S + s * 128 + kk * 8, bdesc, IDESC_O, (j | kk) != 0);
         }
-        umma_commit(P_EMPTY(s));
-        umma_commit(V_EMPTY(s));
-        umma_commit(O_DONE(s));  // one phase per tile of group s
+        umma_commit(V_EMPTY(r));
+        umma_commit(O_DONE);  // one phase per tile
+        // S_{j+2} reuses buffer s: issued after P_j V_j, which the tensor
+        // pipe executes first
+        if (j + 2 < ntiles) issue_s(j + 2);
       }
     }
   } else {
-    // ---------------- softmax warps: two groups ----------------
+    // ---------------- softmax warps: two per TMEM lane quadrant ----------------
     const int quad = warp & 3;
-    const int grp = (warp - 2) >> 2;   // group: key tiles j = grp, grp + 2, ...
+    const int hh = (warp - 2) >> 2;    // key half of every tile (and hd half of Q / O)
     const int row = quad * 32 + lane;  // query row within the tile
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t o_col = TM_O + grp * 128;
-    float m_run = -INFINITY, l_run = 0.f;
-    int last = -1;
-    for (int j = grp; j < ntiles; j += 2) {
-      const int b = grp;  // == j & 1
-      const bool self = j < n_self;
-      const int kvalid = (self ? sd.len - j * KT : sd.ctx_len - (j - n_self) * KT);  // valid keys in tile
-      mbar_wait(S_FULL(b), (j >> 1) & 1);
+    const int qi = q0 + row;
+    const bool row_ok = qi < sd.len;
+    const long off = (long)(sd.tok_start + (row_ok ? qi : 0)) * D + h * HDIM;
+    float* xm = reinterpret_cast<float*>(sm + OFF_X);  // [slot][half][row] maxima
+    float* xl = xm + 4 * 128;                          // [half][row] sums
+    auto pair_sync = [&]() {
+      tc_fence_before();
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory");
       tc_fence_after();
-      uint32_t sr[KT];
+    };
+    // Q (this warp's 64 hd columns of its rows) -> TMEM, packed bf16 pairs
+    {
+      uint32_t qr[32];
 #pragma unroll
-      for (int c = 0; c < KT / 32; ++c)
-        tmem_ld32(tmem + lane_off + TM_S + b * 128 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
-      tmem_wait_ld();
+      for (int u = 0; u < 8; ++u) {
+        const uint4 v = row_ok ? *reinterpret_cast<const uint4*>(a.q + off + hh * 64 + u * 8) : make_uint4(0, 0, 0, 0);
+        qr[4 * u] = v.x;
+        qr[4 * u + 1] = v.y;
+        qr[4 * u + 2] = v.z;
+        qr[4 * u + 3] = v.w;
+      }
+      tmem_st32(tmem + lane_off + TM_Q + hh * 32, qr);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(S_EMPTY(b));  // S buffer may be overwritten now
-      // Row max on the raw scores (the softmax scale is positive); keys past
-      // the sequence end (only in a ragged last tile) become -inf.
-      if (kvalid < KT) {
+      if (lane == 0) mbar_arrive(Q_READY);
+    }
+    float m_run = -INFINITY, l_run = 0.f;
+    for (int j = 0; j < ntiles; ++j) {
+      const int b = j & 1;
+      const int kvalid = (j < n_self ? sd.len - j * KT : sd.ctx_len - (j - n_self) * KT);  // valid keys in tile
+      const int kv_h = kvalid - hh * 64;  // valid keys in this warp's half
+      mbar_wait(S_FULL(b), (j >> 1) & 1);
+      tc_fence_after();
+      uint32_t sr[64];
+      tmem_ld32(tmem + lane_off + TM_S + b * 128 + hh * 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_ld32(tmem + lane_off + TM_S + b * 128 + hh * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      tmem_wait_ld();
+      if (kv_h < 64) {
 #pragma unroll
-        for (int i = 0; i < KT; ++i)
-          if (i >= kvalid) sr[i] = __float_as_uint(-INFINITY);
+        for (int i = 0; i < 64; ++i)
+          if (i >= kv_h) sr[i] = __float_as_uint(-INFINITY);
       }
       float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < KT; i += 4) {
+      for (int i = 0; i < 64; i += 4) {
         mx0 = fmaxf(mx0, __uint_as_float(sr[i]));
         mx1 = fmaxf(mx1, __uint_as_float(sr[i + 1]));
         mx2 = fmaxf(mx2, __uint_as_float(sr[i + 2]));
         mx3 = fmaxf(mx3, __uint_as_float(sr[i + 3]));
       }
-      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.scale_log2;  // log2 domain
-      // conditional rescale of the running max
+      // row max of the whole tile: exchange with the other key half.  The
+      // barrier also orders both halves' S loads before the P stores below
+      // (the other half's P overwrites columns this half has just read).
+      xm[(b * 2 + hh) * 128 + row] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      pair_sync();
+      const float mx = fmaxf(xm[(b * 2) * 128 + row], xm[(b * 2 + 1) * 128 + row]) * a.scale_log2;
+      // conditional rescale of the running max (identical in both halves)
       float corr = 1.f;
-      bool raise = mx > m_run + RESCALE_LOG2 || (m_run == -INFINITY && mx > -INFINITY);
+      const bool raise = mx > m_run + RESCALE_LOG2 || (m_run == -INFINITY && mx > -INFINITY);
       if (raise) {
         corr = m_run == -INFINITY ? 0.f : ex2(m_run - mx);
         m_run = mx;
       }
-      // p = 2^(s * scale - m): one FFMA feeds the exponential
       const float nbase = m_run == -INFINITY ? 0.f : -m_run;
-      // P = exp2(s - m) -> bf16 swizzled tile; row sum in f32
-      mbar_wait(P_EMPTY(b), ((j >> 1) & 1) ^ 1);
-      float rsum = 0.f;
-      uint8_t* prow = sm + OFF_P + b * TILE_BYTES + row * 128;
-#pragma unroll
-      for (int chunk = 0; chunk < KT / 8; ++chunk) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int i = chunk * 8 + 2 * q;
-          const float p0 = ex2(fmaf(__uint_as_float(sr[i]), a.scale_log2, nbase));
-          const float p1 = ex2(fmaf(__uint_as_float(sr[i + 1]), a.scale_log2, nbase));
-          rsum += p0 + p1;
-          __nv_bfloat162 t = __floats2bfloat162_rn(p0, p1);
-          pk[q] = *reinterpret_cast<uint32_t*>(&t);
-        }
-        const int sub = chunk >> 3, cin = chunk & 7;
-        *reinterpret_cast<uint4*>(prow + sub * HALF + ((cin ^ (row & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      }
-      l_run = l_run * corr + rsum;
-      // Rescale O_b (warp-collective) once the previous P.V into O_b is complete.
-      if (__any_sync(0xffffffffu, raise) && j >= 2) {
-        mbar_wait(O_DONE(b), ((j >> 1) - 1) & 1);
+      // Rescale this half's O columns (warp-collective) once the previous
+      // P V has completed.
+      if (__any_sync(0xffffffffu, raise) && j > 0) {
+        mbar_wait(O_DONE, (j - 1) & 1);
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < HDIM / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t r[32];
-          tmem_ld32(tmem + lane_off + o_col + c * 32, r);
+          tmem_ld32(tmem + lane_off + TM_O + hh * 64 + c * 32, r);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
-          tmem_st32(tmem + lane_off + o_col + c * 32, r);
+          tmem_st32(tmem + lane_off + TM_O + hh * 64 + c * 32, r);
         }
-        tmem_wait_st();
       }
-      fence_proxy_async();
+      // P = 2^(s * scale - m) as packed bf16 over this half's score columns
+      // (keys hh*64 + 2c, +1 in column hh*32 + c of the S buffer)
+      uint32_t pk[32];
+      float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const float p0 = ex2(fmaf(__uint_as_float(sr[2 * c]), a.scale_log2, nbase));
+        const float p1 = ex2(fmaf(__uint_as_float(sr[2 * c + 1]), a.scale_log2, nbase));
+        rs0 += p0;
+        rs1 += p1;
+        pk[c] = pack_bf16x2(p0, p1);
+      }
+      tmem_st32(tmem + lane_off + TM_S + b * 128 + hh * 32, pk);
+      tmem_wait_st();
+      l_run = l_run * corr + (rs0 + rs1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(P_FULL(b));
-      last = j;
     }
+
     // prefetch this row's gate half (independent of the attention result)
-    const int qi = q0 + row;
-    const long off = (long)(sd.tok_start + (qi < sd.len ? qi : 0)) * D + h * HDIM;
     uint4 gpre[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u)
-      gpre[u] = (a.gsig && qi < sd.len) ? *reinterpret_cast<const uint4*>(a.gsig + off + grp * 64 + u * 8)
-                                        : make_uint4(0, 0, 0, 0);
-    // this group's last P.V into O_grp
-    if (last >= 0) mbar_wait(O_DONE(grp), (last >> 1) & 1);
+      gpre[u] = (a.gsig && row_ok) ? *reinterpret_cast<const uint4*>(a.gsig + off + hh * 64 + u * 8)
+                                   : make_uint4(0, 0, 0, 0);
+    if (ntiles > 0) mbar_wait(O_DONE, (ntiles - 1) & 1);  // last P V
     tc_fence_after();
-
-    // merge the two groups: exchange (m, l) per row, each group finishes one
-    // 64-column half of hd from both accumulators.  The first barrier (the 8
-    // softmax warps) orders the exchange writes into the Q tile after every
-    // group's final wait: a group without tiles has waited for nothing.
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-    float* xg = reinterpret_cast<float*>(sm + OFF_XCHG);
-    xg[(grp * 2 + 0) * 128 + row] = last >= 0 ? m_run : -INFINITY;
-    xg[(grp * 2 + 1) * 128 + row] = last >= 0 ? l_run : 0.f;
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-    const float m0 = xg[0 * 128 + row], l0 = xg[1 * 128 + row];
-    const float m1 = xg[2 * 128 + row], l1 = xg[3 * 128 + row];
-    const float mm = fmaxf(m0, m1);
-    const float c0 = (mm == -INFINITY || l0 == 0.f) ? 0.f : ex2(m0 - mm);
-    const float c1 = (mm == -INFINITY || l1 == 0.f) ? 0.f : ex2(m1 - mm);
-    const float lsum = l0 * c0 + l1 * c1;
+    xl[hh * 128 + row] = l_run;
+    pair_sync();
+    const float lsum = xl[row] + xl[128 + row];
     const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-    const float w0 = c0 * inv, w1 = c1 * inv;
 #pragma unroll
-    for (int ci = 0; ci < 2; ++ci) {
-      const int c = grp * 2 + ci;
-      uint32_t r0[32], r1[32];
-      tmem_ld32(tmem + lane_off + TM_O + c * 32, r0);
-      tmem_ld32(tmem + lane_off + TM_O + 128 + c * 32, r1);
+    for (int c = 0; c < 2; ++c) {
+      uint32_t r[32];
+      tmem_ld32(tmem + lane_off + TM_O + hh * 64 + c * 32, r);
       tmem_wait_ld();
-      if (qi < sd.len) {
+      if (row_ok) {
 #pragma unroll
-        for (int d0 = 0; d0 < 32; d0 += 8) {
-          float g[8];
-          if (a.gsig) {
-            const uint4 gv = gpre[ci * 4 + d0 / 8];
-            const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gv);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              g[2 * k] = __bfloat162float(gp[k].x);
-              g[2 * k + 1] = __bfloat162float(gp[k].y);
-            }
-          } else {
-#pragma unroll
-            for (int k = 0; k < 8; ++k) g[k] = 1.f;
-          }
+        for (int u = 0; u < 4; ++u) {
+          const uint4 gv = gpre[c * 4 + u];
+          const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gv);
           uint32_t op[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            float v[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int d = d0 + 2 * k + e;
-              // an accumulator that received no tile is never read (w == 0)
-              const float o0 = w0 != 0.f ? __uint_as_float(r0[d]) * w0 : 0.f;
-              const float o1 = w1 != 0.f ? __uint_as_float(r1[d]) * w1 : 0.f;
-              v[e] = (o0 + o1) * g[2 * k + e];
-            }
-            __nv_bfloat162 t = __floats2bfloat162_rn(v[0], v[1]);
-            op[k] = *reinterpret_cast<uint32_t*>(&t);
+            const float g0 = a.gsig ? __bfloat162float(gp[k].x) : 1.f;
+            const float g1 = a.gsig ? __bfloat162float(gp[k].y) : 1.f;
+            op[k] = pack_bf16x2(__uint_as_float(r[u * 8 + 2 * k]) * inv * g0,
+                                __uint_as_float(r[u * 8 + 2 * k + 1]) * inv * g1);
           }
-          *reinterpret_cast<uint4*>(a.out + off + c * 32 + d0) = make_uint4(op[0], op[1], op[2], op[3]);
+          *reinterpret_cast<uint4*>(a.out + off + hh * 64 + c * 32 + u * 8) = make_uint4(op[0], op[1], op[2], op[3]);
         }
       }
     }
@@ -403,7 +389,6 @@ void attention_tc(const AttnParams& p, cudaStream_t s) {
   }
   const long D = (long)p.H * HDIM;
   // copies (the map cache may be cleared between calls)
-  const CUtensorMap mq = tma_map_bf16(p.q, p.rows, D, D, 128);
   const CUtensorMap mk = tma_map_bf16(p.k, p.rows, D, D, 128);
   const CUtensorMap mv = tma_map_bf16(p.v, p.rows, D, D, 128);
   const bool has_ctx = p.ck && p.cv && p.ctx_rows > 0;
@@ -411,12 +396,13 @@ void attention_tc(const AttnParams& p, cudaStream_t s) {
   const CUtensorMap mcv = has_ctx ? tma_map_bf16(p.cv, p.ctx_rows, D, D, 128) : mv;
   TcAttnArgs a;
   a.seqs = p.seqs;
+  a.q = reinterpret_cast<const bf16*>(p.q);
   a.gsig = reinterpret_cast<const bf16*>(p.gsig);
   a.out = reinterpret_cast<bf16*>(p.out);
   a.H = p.H;
   a.scale_log2 = p.scale * 1.4426950408889634f;
   dim3 grid((p.max_len + QT - 1) / QT, p.H, p.nseq);
-  launch_pdl(attn_tc_kernel, grid, dim3(THREADS), SMEM, s, mq, mk, mv, mck, mcv, a);
+  launch_pdl(attn_tc_kernel, grid, dim3(THREADS), SMEM, s, mk, mv, mck, mcv, a);
   IRT_CHECK_LAUNCH();
 }
 
