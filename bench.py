@@ -447,6 +447,8 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # keep stdout to the one JSON line (NCCL prints its version at INFO level)
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
 
