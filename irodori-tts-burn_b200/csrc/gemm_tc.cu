@@ -51,8 +51,11 @@ struct Cfg {
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
-  // stages | barriers (256 B) | one 32x33 f32 transpose buffer per epilogue warp | alignment slack
-  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 256 + EPI_WARPS * 32 * 33 * 4 + 1024;
+  // stages | per-warp epilogue buffers (32x33 f32 transpose, or a 4 KB
+  // 128B-swizzled reduce tile at a 1024-aligned offset) | barriers (256 B) | alignment slack
+  static constexpr uint32_t OFF_EPI = STAGES * STAGE_BYTES;
+  static constexpr uint32_t EPI_BYTES = EPI_WARPS * 32 * 33 * 4;
+  static constexpr size_t SMEM = (size_t)OFF_EPI + EPI_BYTES + 256 + 1024;
   // instruction descriptor, kind::f16: D=f32 (bit4), A=B=bf16 (bits 7,10), K-major
   // both, N>>3 at bits 17-22, M>>4 at bits 24-28 (M = 128 per CTA of the group).
   static constexpr uint32_t IDESC =
@@ -166,6 +169,19 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_rank0), "r"(c0), "r"(c1)
       : "memory");
 }
+// TMA reduce-add of a shared-memory box into global memory (f32 add performed
+// atomically by the memory system), bulk-group completion.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
@@ -222,15 +238,16 @@ struct Regs {
 // walks the same work units, rank 0 issues the MMAs for both.
 template <int BN, int CG>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
-                int splits, const __grid_constant__ EpiParams ep) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmX, int M, int N, int K, int splits,
+                const __grid_constant__ EpiParams ep) {
   using C = Cfg<BN, CG>;
   constexpr int STAGES = C::STAGES;
   constexpr int BMT = BM * CG;  // rows of one work tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_EPI + C::EPI_BYTES);
   // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2]; then tmem base slot
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
 
@@ -401,11 +418,50 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_wait_ld();
           if (row_ok) epi_chunk_swiglu<Regs<64>, true>(ep, row, n0 + c, R);
         }
+      } else if (ep.mode == EPI_RESID && ep.x_tma) {
+        // Gated residual x += gate * acc without reading x: each 32 x 32 chunk
+        // of gate * acc goes to a 128B-swizzled shared-memory tile and one TMA
+        // reduce-add folds it into x (also for K-splits: the adds are atomic).
+        float* xb = reinterpret_cast<float*>(smem + C::OFF_EPI + (warp - 2) * 4096);
+#pragma unroll 1
+        for (int c = 32 * half; c < BN; c += 64) {
+          if (n0 + c >= N) break;
+          Regs<32> R;
+          tmem_ld32(taddr, R.r, c);
+          float g[32];
+          if (ep.gate) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 gv = *reinterpret_cast<const float4*>(ep.gate + n0 + c + 4 * q);
+              g[4 * q] = gv.x;
+              g[4 * q + 1] = gv.y;
+              g[4 * q + 2] = gv.z;
+              g[4 * q + 3] = gv.w;
+            }
+          } else {
+#pragma unroll
+            for (int q = 0; q < 32; ++q) g[q] = 1.f;
+          }
+          tmem_wait_ld();
+          if (lane == 0) bulk_wait_read0();  // the previous reduce has read xb
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(xb + lane * 32 + ((q ^ (lane & 7)) << 2)) =
+                make_float4(g[4 * q] * R(4 * q), g[4 * q + 1] * R(4 * q + 1), g[4 * q + 2] * R(4 * q + 2),
+                            g[4 * q + 3] * R(4 * q + 3));
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_reduce_add_2d(&tmX, smem_u32(xb), n0 + c, m0 + quad * 32);
+            bulk_commit();
+          }
+        }
       } else if (ep.mode == EPI_RESID) {
         // Gated residual x += gate * acc through a per-warp 32x32 shared-memory
         // transpose: lane l then owns column l, so every warp access to the f32
         // residual stream is 128 contiguous bytes of one row (coalesced RMW).
-        float* stg = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES + 256) + (warp - 2) * (32 * 33);
+        float* stg = reinterpret_cast<float*>(smem + C::OFF_EPI) + (warp - 2) * (32 * 33);
 #pragma unroll 1
         for (int c = 32 * half; c < BN; c += 64) {
           if (n0 + c >= N) break;
@@ -457,6 +513,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   }
 
+  // reduces issued by this thread have read their shared memory and completed
+  if (warp >= 2 && lane == 0) bulk_wait0();
   __syncthreads();
   // a pair stays resident until neither CTA signals the other any more
   if constexpr (CG == 2) cluster_sync();
@@ -526,6 +584,22 @@ const CUtensorMap& tensor_map(const void* p, long rows, long cols, long ld, int 
   return cache.emplace(key, m).first->second;
 }
 
+// f32 2-D tensor map of the residual stream for the epilogue's TMA
+// reduce-add: 32 x 32 box (128-byte rows), 128-byte swizzle.  Encoded per
+// launch (a host-side table fill).
+CUtensorMap tensor_map_resid(const float* p, long rows, long cols, long ld) {
+  CUtensorMap m;
+  cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t gstride[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = get_encode()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), gdim, gstride, box,
+                            estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error(IRT_E_CUDA, "cuTensorMapEncodeTiled (f32) failed (" + std::to_string((int)r) + ")");
+  return m;
+}
+
 int num_sms() {
   static int n = 0;
   if (!n) {
@@ -579,10 +653,17 @@ void launch(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int 
   }
   const CUtensorMap ta = tensor_map(A, M, K, lda, BM);  // copies: the cache may be cleared
   const CUtensorMap tb = tensor_map(B, N, K, ldb, C::B_ROWS);
+  // residual by TMA reduce-add (not for row-masked residuals)
+  const bool xtma = p.mode == EPI_RESID && !p.row_scale && p.x && (N % 32) == 0 &&
+                    (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 &&
+                    (!p.gate || (reinterpret_cast<uintptr_t>(p.gate) & 15) == 0);
+  const CUtensorMap tx = xtma ? tensor_map_resid(p.x, M, N, N) : ta;
+  EpiParams pp = p;
+  pp.x_tma = xtma ? 1 : 0;
   const int units = ((M + BM * CG - 1) / (BM * CG)) * ((N + BN - 1) / BN) * splits;
   if constexpr (CG == 1) {
     const int grid = units < num_sms() ? units : num_sms();
-    launch_pdl(gemm_kernel<BN, 1>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, M, N, K, splits, p);
+    launch_pdl(gemm_kernel<BN, 1>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, tx, M, N, K, splits, pp);
   } else {
     const int pairs = std::min(units, max_pairs<BN>());
     cudaLaunchConfig_t cfg = {};
@@ -599,7 +680,7 @@ void launch(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
-    IRT_CUDA(cudaLaunchKernelEx(&cfg, gemm_kernel<BN, 2>, ta, tb, M, N, K, splits, p));
+    IRT_CUDA(cudaLaunchKernelEx(&cfg, gemm_kernel<BN, 2>, ta, tb, tx, M, N, K, splits, pp));
   }
   IRT_CHECK_LAUNCH();
 }

@@ -52,6 +52,7 @@ struct EpiParams {
   // RESID
   float* x = nullptr;
   const float* gate = nullptr;    // [N] or null (= 1)
+  int x_tma = 0;                   // RESID on tcgen05: the launcher attached a reduce-add tensor map of x
   // SWIGLU
   void* h = nullptr;              // [M, F]
   int F = 0;
