@@ -163,6 +163,13 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
+def measured_sustained():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()).get("bf16_tflops_sustained")
+    return None
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -531,6 +538,10 @@ def main():
             "frac": round(achieved / peak, 4), "traffic": None,
             "kernel": "gemm_kernel<256> (tcgen05), 4 DiT GEMMs of one layer at M=%d" % (2 * ntok),
             "peak_kind": f"{peak_kind} burst bf16"}
+    sust = measured_sustained()
+    if sust:
+        # the GPU runs power-capped after the timed region; for reference only
+        roof["frac_of_sustained_peak"] = round(achieved / sust, 4)
     total_flops = job_flops(utts)
     extra = {"job_tflop": round(total_flops / 1e12, 2),
              "job_tflops_achieved": round(total_flops * args.steps / (ms / 1000.0) / 1e12, 1)}
