@@ -236,8 +236,10 @@ void Engine::load(const std::string& path) {
   cm2.alloc((size_t)3 * D * D * 4);
   upload_rows(stg, lin("cond_module.linear2.weight", 3 * D, D), cm2.p, 0, D, 0, 0, 0);
 
-  in_w.alloc((size_t)D * P * es);
-  upload_rows(stg, lin("in_proj.weight", D, P), in_w.p, bf, P, 0, 0, 0);
+  Pk = (bf && P % 64) ? (P + 63) / 64 * 64 : P;
+  in_w.alloc((size_t)D * Pk * es);
+  IRT_CUDA(cudaMemset(in_w.p, 0, (size_t)D * Pk * es));  // zero K padding
+  upload_rows(stg, lin("in_proj.weight", D, P), in_w.p, bf, Pk, 0, 0, 0);
   f32vec(in_b, "in_proj.bias", D);
 
   const char* kinds[3] = {"shift", "scale", "gate"};
@@ -487,7 +489,7 @@ void Engine::dit_forward(int M, const SeqDesc* d_seqs, int nseq, int max_len, co
     p.out = x;
     p.ldo = D;
     p.bias = in_b.as<float>();
-    gemm(ws.xin.p, P, in_w, M, D, P, p, s);
+    gemm(ws.xin.p, Pk, in_w, M, D, Pk, p, s);
   }
   float* dump = dump_layers;
   if (dump) {
@@ -904,7 +906,8 @@ void Engine::sample(const irt_request& rq, float* out, int out_memory, cudaStrea
   ws.g.ensure((size_t)Mmax * D * esz());
   ws.attn.ensure((size_t)Mmax * D * esz());
   ws.hm.ensure((size_t)Mmax * F * esz());
-  ws.xin.ensure((size_t)Mmax * P * esz());
+  ws.xin.ensure((size_t)Mmax * Pk * esz());
+  if (Pk != P) IRT_CUDA(cudaMemsetAsync(ws.xin.p, 0, (size_t)Mmax * Pk * esz(), s));  // zero K padding
   ws.vout.ensure((size_t)Mmax * P * 4);
   ws.tokpos.ensure((size_t)Mmax * 4);
   {
@@ -1008,7 +1011,7 @@ void Engine::sample(const irt_request& rq, float* out, int out_memory, cudaStrea
     int toff = table_off.at(groups);
     // replicate x into each group's rows
     for (int g = 0; g < G; ++g)
-      gather_rows(xin_f32, nullptr, ws.xin.as<uint8_t>() + (size_t)g * ntok * P * esz(), bf, ntok, P, s);
+      gather_rows(xin_f32, nullptr, ws.xin.as<uint8_t>() + (size_t)g * ntok * Pk * esz(), bf, ntok, P, s, Pk);
     forward_step(G * ntok, ws.seqs.as<SeqDesc>() + toff, G * B, Smax, t_index, nctx, s);
     last_row_forwards += (long long)G * B;
     if (G == 1) {

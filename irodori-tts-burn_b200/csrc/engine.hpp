@@ -46,6 +46,9 @@ struct Engine {
 
   // dimensions
   int D = 0, L = 0, H = 0, hd = 0, P = 0, F = 0, Fp = 0, R = 0, Temb = 0;
+  // in_proj reduction width: P, or (bf16 mode) P zero-padded to a multiple of
+  // 64 so the projection runs on the tcgen05 GEMM with its bias epilogue
+  int Pk = 0;
   int aux_kind = 0;  // 0 none, 1 speaker, 2 caption
   int aux_dim = 0;
 

@@ -130,7 +130,9 @@ void embed_rows(const int* ids, const uint8_t* mask, const float* table, float* 
 void embed_rows_v(const int* ids, const uint8_t* mask, const float* table, float* x, int M, int D, int vocab,
                   cudaStream_t s);
 // out[m] = convert(in[m]) for f32 -> bf16/f32 copies with optional row gather
-void gather_rows(const float* in, const int* src_row, void* out, int out_bf16, int M, int D, cudaStream_t s);
+// out row m (row stride ld_out, default D) = in row src_row[m] (or m), converted.
+void gather_rows(const float* in, const int* src_row, void* out, int out_bf16, int M, int D, cudaStream_t s,
+                 int ld_out = 0);
 // scale rows by a mask (x *= mask[m])
 void mask_rows(float* x, const uint8_t* mask, int M, int D, cudaStream_t s);
 void silu_copy(const float* in, long ld_in, float* out, long ld_out, int M, int D, cudaStream_t s);

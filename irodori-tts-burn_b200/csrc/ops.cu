@@ -240,14 +240,15 @@ __global__ void embed_kernel(const int* ids, const uint8_t* mask, const float* t
   x[i] = table[(long)id * D + d] * mk;
 }
 
-__global__ void gather_kernel(const float* in, const int* src, void* out, int out_bf16, int M, int D) {
+__global__ void gather_kernel(const float* in, const int* src, void* out, int out_bf16, int M, int D, int ldo) {
   long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long)M * D) return;
   int m = (int)(i / D), d = (int)(i % D);
   int r = src ? src[m] : m;
   float v = in[(long)r * D + d];
-  if (out_bf16) reinterpret_cast<bf16*>(out)[i] = __float2bfloat16_rn(v);
-  else reinterpret_cast<float*>(out)[i] = v;
+  const long o = (long)m * ldo + d;
+  if (out_bf16) reinterpret_cast<bf16*>(out)[o] = __float2bfloat16_rn(v);
+  else reinterpret_cast<float*>(out)[o] = v;
 }
 
 __global__ void mask_rows_kernel(float* x, const uint8_t* mask, int M, int D) {
@@ -393,9 +394,10 @@ void embed_rows_v(const int* ids, const uint8_t* mask, const float* table, float
 void embed_rows(const int* ids, const uint8_t* mask, const float* table, float* x, int M, int D, cudaStream_t s) {
   embed_rows_v(ids, mask, table, x, M, D, 1 << 30, s);
 }
-void gather_rows(const float* in, const int* src_row, void* out, int out_bf16, int M, int D, cudaStream_t s) {
+void gather_rows(const float* in, const int* src_row, void* out, int out_bf16, int M, int D, cudaStream_t s,
+                 int ld_out) {
   if ((long)M * D == 0) return;
-  gather_kernel<<<nblk((long)M * D), 256, 0, s>>>(in, src_row, out, out_bf16, M, D);
+  gather_kernel<<<nblk((long)M * D), 256, 0, s>>>(in, src_row, out, out_bf16, M, D, ld_out > 0 ? ld_out : D);
   IRT_CHECK_LAUNCH();
 }
 void mask_rows(float* x, const uint8_t* mask, int M, int D, cudaStream_t s) {
