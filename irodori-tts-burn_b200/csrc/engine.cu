@@ -307,6 +307,11 @@ void Engine::load(const std::string& path) {
   f32vec(out_norm, "out_norm.weight", D);
   out_w.alloc((size_t)P * D * es);
   upload_rows(stg, lin("out_proj.weight", P, D), out_w.p, bf, D, 0, 0, 0);
+  if (bf && P <= 128) {
+    out_w_pad.alloc((size_t)128 * D * es);
+    IRT_CUDA(cudaMemset(out_w_pad.p, 0, (size_t)128 * D * es));
+    IRT_CUDA(cudaMemcpy(out_w_pad.p, out_w.p, (size_t)P * D * es, cudaMemcpyDeviceToDevice));
+  }
   f32vec(out_b, "out_proj.bias", P);
   IRT_CUDA(cudaDeviceSynchronize());
 }
@@ -546,7 +551,20 @@ void Engine::dit_forward(int M, const SeqDesc* d_seqs, int nseq, int max_len, co
                                cudaMemcpyDeviceToDevice, s));
   }
   // out_norm + out_proj fused (narrow N = P): one pass over x per row
-  rmsnorm_proj(x, out_norm.as<float>(), out_w.p, bf, out_b.as<float>(), ws.vout.as<float>(), M, D, P, eps, s);
+  EpiParams op;
+  op.mode = EPI_STORE;
+  op.M = M;
+  op.N = P;  // columns stored; the GEMM runs 128 wide over the padded weight
+  op.out = ws.vout.p;
+  op.ldo = P;
+  op.bias = out_b.as<float>();
+  if (out_w_pad.p && M >= 128 && (D % 64) == 0) {
+    // out_norm (RmsNorm, bf16 rows) then out_proj on the tensor cores
+    rms_norm(x, out_norm.as<float>(), ws.h.p, 1, M, D, eps, s);
+    gemm_tc(ws.h.as<bf16>(), D, out_w_pad.as<bf16>(), D, M, 128, D, op, s);
+  } else {
+    rmsnorm_proj(x, out_norm.as<float>(), out_w.p, bf, out_b.as<float>(), ws.vout.as<float>(), M, D, P, eps, s);
+  }
 }
 
 // ---------------------------------------------------------------------------

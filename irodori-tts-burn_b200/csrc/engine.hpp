@@ -61,6 +61,10 @@ struct Engine {
   DevBuf ctx_text_w, ctx_aux_w;       // [L*2D, td] / [L*2D, ad]: per layer [Wk; Wv]
   DevBuf kn_all;                      // f32 [L, D]
   DevBuf out_norm, out_w, out_b;
+  // bf16 mode: out_proj rows zero-padded to 128 so the projection of the
+  // normalised rows runs on the tcgen05 GEMM (only the first P columns are
+  // stored)
+  DevBuf out_w_pad;
 
   // workspaces (grow-only)
   struct WS {
