@@ -202,6 +202,40 @@ std::vector<float> up_f32(DevBuf& dst, const TensorView& v) {
   return h;
 }
 
+void up_host(DevBuf& dst, const std::vector<float>& h) {
+  dst.alloc(h.size() * 4 + 4);
+  IRT_CUDA(cudaMemcpy(dst.p, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
+}
+
+// Rank-3 convolution weight `<p>.weight`, or its weight-norm parametrisation
+// `<p>.weight_g` / `<p>.weight_v` resolved at load exactly as the reference's
+// converter does (scripts/convert_dacvae_weights.py:39-70):
+//   weight = g * v / (||v|| + 1e-12), ||v|| over all dimensions except dim 0.
+std::vector<float> conv_weight(const SafeTensorsFile& st, const std::string& p, std::vector<long>& shape) {
+  if (st.has(p + ".weight") || !(st.has(p + ".weight_g") && st.has(p + ".weight_v"))) {
+    const TensorView& w = st.get(p + ".weight", 3);
+    shape.assign(w.shape.begin(), w.shape.end());
+    std::vector<float> h((size_t)w.numel());
+    decode_to_f32(w, h.data());
+    return h;
+  }
+  const TensorView& v = st.get(p + ".weight_v", 3);
+  const TensorView& g = st.get(p + ".weight_g");
+  shape.assign(v.shape.begin(), v.shape.end());
+  const long rows = shape[0], per = (long)v.numel() / rows;
+  if (g.numel() != rows) throw shape_error(p + ".weight_g must hold one magnitude per output index");
+  std::vector<float> h((size_t)v.numel()), gh((size_t)rows);
+  decode_to_f32(v, h.data());
+  decode_to_f32(g, gh.data());
+  for (long r = 0; r < rows; ++r) {
+    double ss = 0.0;
+    for (long i = 0; i < per; ++i) ss += (double)h[r * per + i] * h[r * per + i];
+    const float scale = gh[r] / ((float)std::sqrt(ss) + 1e-12f);
+    for (long i = 0; i < per; ++i) h[r * per + i] *= scale;
+  }
+  return h;
+}
+
 void up_bf16(DevBuf& dst, const std::vector<uint16_t>& h) {
   dst.alloc(h.size() * 2 + 16);
   IRT_CUDA(cudaMemcpy(dst.p, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
@@ -239,13 +273,14 @@ Codec::Codec(int dev, const std::string& path, int precision) : device(dev), pre
   SafeTensorsFile st(path);
   auto get = [&](const std::string& k, size_t rank) -> const TensorView& { return st.get(k, rank); };
   auto conv = [&](Conv& c, const std::string& p, int dil) {
-    const TensorView& w = get(p + ".weight", 3);
-    c.cout = (int)w.shape[0];
-    c.cin = (int)w.shape[1];
-    c.k = (int)w.shape[2];
+    std::vector<long> shp;
+    std::vector<float> h = conv_weight(st, p, shp);
+    c.cout = (int)shp[0];
+    c.cin = (int)shp[1];
+    c.k = (int)shp[2];
     c.dil = dil;
     c.pad = (c.k - 1) * dil / 2;  // conv_pad(k, 1, dil) (src/codec/layers.rs:64-66)
-    std::vector<float> h = up_f32(c.w, w);
+    up_host(c.w, h);
     if (st.has(p + ".bias")) up_f32(c.b, get(p + ".bias", 1));
     if (prec == IRT_PREC_BF16 && c.cout % 32 == 0 && c.cin % 8 == 0) {
       c.cin_pad = round_up64(c.cin);
@@ -260,13 +295,14 @@ Codec::Codec(int dev, const std::string& path, int precision) : device(dev), pre
     std::string p = "decoder.model." + std::to_string(i + 1);
     bl.stride = rates[i];
     up_f32(bl.alpha, get(p + ".block.0.alpha", 3));
-    const TensorView& w = get(p + ".block.1.weight", 3);
-    bl.ct.cin = (int)w.shape[0];
-    bl.ct.cout = (int)w.shape[1];
-    bl.ct.k = (int)w.shape[2];
+    std::vector<long> shp;
+    std::vector<float> h = conv_weight(st, p + ".block.1", shp);  // [cin, cout, 2s]
+    bl.ct.cin = (int)shp[0];
+    bl.ct.cout = (int)shp[1];
+    bl.ct.k = (int)shp[2];
     if (bl.ct.k != 2 * bl.stride) throw shape_error(p + ".block.1.weight kernel != 2*stride");
     bl.ct.pad = (bl.stride + 1) / 2;  // conv_transpose_pad (src/codec/layers.rs:71-75)
-    std::vector<float> h = up_f32(bl.ct.w, w);
+    up_host(bl.ct.w, h);
     if (st.has(p + ".block.1.bias")) up_f32(bl.ct.b, get(p + ".block.1.bias", 1));
     if (prec == IRT_PREC_BF16 && bl.ct.cout % 32 == 0 && bl.ct.cin % 8 == 0 && bl.stride >= 2) {
       bl.ct.cin_pad = round_up64(bl.ct.cin);

@@ -239,8 +239,29 @@ def codec_param_shapes(width_div: int = 1) -> Dict[str, tuple]:
     return s
 
 
+def weight_norm_split(tensors: Dict[str, torch.Tensor], seed: int = 11) -> Dict[str, torch.Tensor]:
+    """Store every rank-3 ``X.weight`` as the PyTorch weight-norm pair
+    ``X.weight_g`` [dim0, 1, 1] / ``X.weight_v`` (same shape) that resolves to
+    it (g * v / ||v||, norm over all dims but 0; the form the reference's
+    converter, scripts/convert_dacvae_weights.py, consumes).  v is the weight
+    scaled by a random positive factor per dim-0 index."""
+    gen = torch.Generator()
+    gen.manual_seed(seed)
+    out: Dict[str, torch.Tensor] = {}
+    for k, w in tensors.items():
+        if k.endswith(".weight") and w.dim() == 3:
+            wf = w.float()
+            c = 0.5 + 1.5 * torch.rand((wf.shape[0], 1, 1), generator=gen)
+            out[k[:-len(".weight")] + ".weight_v"] = (wf * c).to(w.dtype)
+            out[k[:-len(".weight")] + ".weight_g"] = wf.flatten(1).norm(dim=1).reshape(-1, 1, 1).to(w.dtype)
+        else:
+            out[k] = w
+    return out
+
+
 def make_codec_checkpoint(path: str, seed: int = 5, width_div: int = 1,
-                          dtype: torch.dtype = torch.float32, init: str = "weightnorm") -> None:
+                          dtype: torch.dtype = torch.float32, init: str = "weightnorm",
+                          weight_norm: bool = False) -> None:
     """Random decoder weights.
 
     ``init="reference"``: the reference's own random initialisation of codec
@@ -266,6 +287,8 @@ def make_codec_checkpoint(path: str, seed: int = 5, width_div: int = 1,
                 bound = 1.0 / math.sqrt(fan_in)
                 t = (torch.rand(shape, generator=gen) * 2 - 1) * bound
             tensors[name] = t.to(dtype)
+        if weight_norm:
+            tensors = weight_norm_split(tensors)
         write_safetensors(path, tensors, {"config_json": json.dumps({})})
         return
     for name, shape in sorted(shapes.items()):
@@ -279,6 +302,8 @@ def make_codec_checkpoint(path: str, seed: int = 5, width_div: int = 1,
             norm = v.flatten(1).norm(dim=1).reshape(-1, 1, 1)
             t = g * v / norm
         tensors[name] = t.to(dtype)
+    if weight_norm:
+        tensors = weight_norm_split(tensors)
     write_safetensors(path, tensors, {"config_json": json.dumps({})})
 
 

@@ -129,3 +129,21 @@ def test_codec_bf16_tc_matches_f32(gpu, pkg, full_codec_path, B, T, lens):
         err = rel_l2(o[:n * hop], r[:n * hop])
         print(f"B={B} T={T} utt {b} len {n}: rel L2 {err:.3e}, SNR {snr_db(o[:n * hop], r[:n * hop]):.1f} dB")
         assert err < BF16_TOL, (b, err)
+
+
+def test_codec_weight_norm_checkpoint_resolved_at_load(gpu, pkg, synth, tmp_path):
+    """A checkpoint holding the weight-norm parametrisation (X.weight_g /
+    X.weight_v) decodes like the resolved one (scripts/convert_dacvae_weights.py
+    resolution applied at load), in both precisions."""
+    merged = tmp_path / "merged.safetensors"
+    wn = tmp_path / "weight_norm.safetensors"
+    synth.make_codec_checkpoint(str(merged), seed=5, width_div=1, init="reference")
+    synth.make_codec_checkpoint(str(wn), seed=5, width_div=1, init="reference", weight_norm=True)
+    lat = torch.randn(1, 5, 32, generator=torch.Generator().manual_seed(13))
+    # f32: the resolution itself (last-bit differences only); bf16: weights that
+    # differ in their last f32 bits round to bf16 differently, so the two decodes
+    # differ by about the bf16 error itself -- bounded like any bf16 decode
+    for prec, tol in (("f32", 1e-5), ("bf16", BF16_TOL)):
+        a = pkg.load_codec(str(merged), device=0, precision=prec).decode(lat)
+        b = pkg.load_codec(str(wn), device=0, precision=prec).decode(lat)
+        assert rel_l2(b, a) < tol, (prec, rel_l2(b, a))
