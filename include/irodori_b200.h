@@ -150,6 +150,14 @@ typedef struct irt_engine irt_engine;
  * does, src/model/attention.rs:514-523, src/model/feed_forward.rs:96-103).
  * The engine starts in the Loaded state with no sampling parameters. */
 IRT_API int irt_engine_create(int device, const char* safetensors_path, int precision, irt_engine** out);
+/* InferenceBuilder::load_weights_with_adapter(path, adapter_dir) (feature
+ * "lora", src/inference.rs:118-139): as irt_engine_create, with the PEFT LoRA
+ * adapter in adapter_dir (adapter_config.json + adapter_model.safetensors)
+ * merged into the base weights at load, W += (lora_alpha / r) * B A, and each
+ * merged weight re-encoded to its checkpoint dtype (src/lora.rs:205-322,
+ * src/weights/tensor_store.rs:62-118). */
+IRT_API int irt_engine_create_with_adapter(int device, const char* safetensors_path, const char* adapter_dir,
+                                           int precision, irt_engine** out);
 /* Drop. */
 IRT_API int irt_engine_destroy(irt_engine* e);
 /* with_sampling(params) (src/inference.rs:151-155, :166-172, :231-233):

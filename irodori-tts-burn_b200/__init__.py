@@ -98,6 +98,8 @@ _SIGNATURES = {
     "irt_sampler_params_default": (None, [ctypes.POINTER(_Params)]),
     "irt_sampler_params_validate": (ctypes.c_int, [ctypes.POINTER(_Params)]),
     "irt_engine_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]),
+    "irt_engine_create_with_adapter": (ctypes.c_int, [ctypes.c_int, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int,
+                                                      ctypes.POINTER(ctypes.c_void_p)]),
     "irt_engine_destroy": (ctypes.c_int, [ctypes.c_void_p]),
     "irt_engine_set_sampling": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(_Params)]),
     "irt_engine_set_default_sampling": (ctypes.c_int, [ctypes.c_void_p]),
@@ -304,6 +306,17 @@ class InferenceBuilder:
             raise IrodoriError(22, f"unknown precision {precision!r}")
         h = ctypes.c_void_p()
         _check(lib().irt_engine_create(self._device, str(path).encode(), PREC[precision], ctypes.byref(h)))
+        return LoadedBuilder(_Handle(h), self._device, precision)
+
+    def load_weights_with_adapter(self, path: str, adapter_dir: str, precision: str = "bf16") -> "LoadedBuilder":
+        """Load a checkpoint and merge a PEFT LoRA adapter directory
+        (adapter_config.json + adapter_model.safetensors) into its weights at
+        load (src/inference.rs:118-139)."""
+        if precision not in PREC:
+            raise IrodoriError(22, f"unknown precision {precision!r}")
+        h = ctypes.c_void_p()
+        _check(lib().irt_engine_create_with_adapter(self._device, str(path).encode(), str(adapter_dir).encode(),
+                                                    PREC[precision], ctypes.byref(h)))
         return LoadedBuilder(_Handle(h), self._device, precision)
 
 

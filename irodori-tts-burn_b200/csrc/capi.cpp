@@ -82,6 +82,19 @@ int irt_engine_create(int device, const char* path, int precision, irt_engine** 
   });
 }
 
+int irt_engine_create_with_adapter(int device, const char* path, const char* adapter_dir, int precision,
+                                   irt_engine** out) {
+  return guard([&] {
+    need(path, "safetensors_path");
+    need(adapter_dir, "adapter_dir");
+    need(out, "out");
+    *out = nullptr;
+    auto h = std::make_unique<irt_engine>();
+    h->e = std::make_unique<irt::Engine>(device, path, precision, adapter_dir);
+    *out = h.release();
+  });
+}
+
 int irt_engine_destroy(irt_engine* e) {
   return guard([&] { delete e; });
 }

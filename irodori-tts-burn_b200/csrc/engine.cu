@@ -1,6 +1,7 @@
 // Engine implementation: checkpoint upload + packing, condition encoders,
 // context KV cache, precomputed adaLN tables, DiT forward and the RF sampler.
 #include "engine.hpp"
+#include "lora.hpp"
 
 #include <algorithm>
 #include <cmath>
@@ -92,13 +93,14 @@ void rope_tables_host(int hd, int S, std::vector<float>& cs, std::vector<float>&
 // Construction / weight loading
 // ---------------------------------------------------------------------------
 
-Engine::Engine(int dev, const std::string& path, int precision) : device(dev), prec(precision) {
+Engine::Engine(int dev, const std::string& path, int precision, const std::string& adapter_dir)
+    : device(dev), prec(precision) {
   if (precision != IRT_PREC_BF16 && precision != IRT_PREC_F32) throw Error(IRT_E_INVALID_ARG, "invalid precision");
   bf = precision == IRT_PREC_BF16;
   use_graphs = std::getenv("IRT_NO_GRAPHS") == nullptr;
   IRT_CUDA(cudaSetDevice(dev));
   IRT_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
-  load(path);
+  load(path, adapter_dir);
 }
 
 Engine::~Engine() {
@@ -165,8 +167,9 @@ void Engine::load_encoder(const SafeTensorsFile& st, EncoderW& e, const std::str
   }
 }
 
-void Engine::load(const std::string& path) {
+void Engine::load(const std::string& path, const std::string& adapter_dir) {
   SafeTensorsFile st(path);
+  if (!adapter_dir.empty()) lora_merged = (int)apply_lora(st, adapter_dir).size();
   const std::string* cj = st.meta("config_json");
   if (!cj) throw Error(IRT_E_NO_CONFIG, "Checkpoint is missing the 'config_json' metadata key");
   cfg = ModelConfig::from_json(*cj);

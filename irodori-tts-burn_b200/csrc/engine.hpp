@@ -98,7 +98,9 @@ struct Engine {
   void forward_step(int M, const SeqDesc* d_seqs, int nseq, int max_len, int t_index, int nrows_ctx,
                     cudaStream_t s);
 
-  Engine(int dev, const std::string& path, int precision);
+  // adapter_dir: optional PEFT LoRA adapter merged into the weights at load
+  Engine(int dev, const std::string& path, int precision, const std::string& adapter_dir = "");
+  int lora_merged = 0;  // base weights updated by the adapter
   ~Engine();
 
   void sample(const irt_request& req, float* out, int out_memory, cudaStream_t user_stream);
@@ -112,7 +114,7 @@ struct Engine {
                    cudaStream_t s);
 
  private:
-  void load(const std::string& path);
+  void load(const std::string& path, const std::string& adapter_dir);
   void load_encoder(const SafeTensorsFile& st, EncoderW& e, const std::string& prefix, int dim, int heads,
                     int layers, double ratio, bool embedding, int vocab, int in_dim);
 };

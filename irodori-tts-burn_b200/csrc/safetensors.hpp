@@ -128,7 +128,29 @@ class SafeTensorsFile {
   }
   const std::map<std::string, TensorView>& tensors() const { return tensors_; }
 
+  // In-memory edits used when an adapter is merged at load: replace a
+  // tensor by owned f32 data, rename or drop an entry.
+  void override_f32(const std::string& k, std::vector<float> data, const std::vector<int64_t>& shape) {
+    std::vector<float>& buf = owned_[k];
+    buf = std::move(data);
+    TensorView v;
+    v.dtype = DType::F32;
+    v.dtype_name = "F32";
+    v.shape = shape;
+    v.data = reinterpret_cast<const uint8_t*>(buf.data());
+    v.nbytes = buf.size() * 4;
+    tensors_[k] = v;
+  }
+  void rename(const std::string& from, const std::string& to) {
+    auto it = tensors_.find(from);
+    if (it == tensors_.end() || from == to) return;
+    tensors_[to] = it->second;
+    tensors_.erase(from);
+  }
+  void erase(const std::string& k) { tensors_.erase(k); }
+
  private:
+  std::map<std::string, std::vector<float>> owned_;
   int fd_ = -1;
   const uint8_t* base_ = nullptr;
   size_t size_ = 0;
