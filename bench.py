@@ -256,30 +256,49 @@ def gemm_roofline(M, reps=5):
 # CPU leg: the oracle (restatement of the reference path) on the host cores
 # ---------------------------------------------------------------------------
 
-def attn_case(steps):
-    """Profiling case: the joint attention of one DiT layer at the config-3
-    CFG step (cond row: 750 queries over 750 self + 576 context keys; uncond
-    row: 750 over 750), H = 16, hd = 128, bf16, through the tcgen05 kernel;
-    `steps` launches timed with CUDA events.  Returns (ms per launch, TFLOP/s)."""
+def attn_case(steps, which="c3"):
+    """Profiling case: the joint attention of one DiT layer, H = 16, hd = 128,
+    bf16, through the tcgen05 kernel; `steps` launches timed with CUDA events.
+    "c3": the config-3 CFG step (cond row: 750 queries over 750 self + 576
+    context keys; uncond row: 750 over 750).  "c4": the config-4 CFG step
+    (64 utterances; cond rows over self + text + speaker keys, uncond rows over
+    self keys), packed (group, utterance, frame) like the engine.  "c4p": the
+    config-4 plain step (cond rows only).  Returns (ms per launch, TFLOP/s)."""
     import torch
     L = ctypes.CDLL(str(PKG_DIR / "libirodori_b200_testhooks.so"))
     L.irtt_attention.argtypes = ([ctypes.c_void_p] * 8 + [ctypes.c_int] * 3 + [ctypes.c_void_p] + [ctypes.c_int] * 4)
     L.irtt_last_error.restype = ctypes.c_char_p
     L.irtt_attention_async.argtypes = L.irtt_attention.argtypes
     dev = torch.device("cuda")
-    H, hd, S, C = 16, 128, 750, 576
+    H, hd = 16, 128
     D = H * hd
+    if which in ("c4", "c4p"):
+        utts = workload()
+        lens = [u[1] for u in utts]
+        ctxs = [u[0] + u[2] + 1 for u in utts]
+    else:
+        lens, ctxs = [750], [576]
+    uncond = which != "c4p"
+    seqs, tok, co = [], 0, 0
+    for S, c in zip(lens, ctxs):  # cond rows
+        seqs.append((tok, S, co, c))
+        tok, co = tok + S, co + c
+    for S in (lens if uncond else []):  # uncond rows
+        seqs.append((tok, S, 0, 0))
+        tok += S
+    rows, C = tok, co
     g = torch.Generator(device=dev).manual_seed(0)
-    mk = lambda n: torch.randn(n, D, device=dev, generator=g).to(torch.bfloat16)  # noqa: E731
-    q, k, v, ck_, cv = mk(2 * S), mk(2 * S), mk(2 * S), mk(C), mk(C)
-    gs = torch.sigmoid(torch.randn(2 * S, D, device=dev, generator=g)).to(torch.bfloat16)
-    out = torch.empty(2 * S, D, device=dev, dtype=torch.bfloat16)
-    seqs = [(0, S, 0, C), (S, S, 0, 0)]
-    sd = (ctypes.c_int * 8)(*[x for t in seqs for x in t])
+    mk = lambda m: torch.randn(m, D, device=dev, generator=g).to(torch.bfloat16)  # noqa: E731
+    q, k, v, ck_, cv = mk(rows), mk(rows), mk(rows), mk(max(C, 128)), mk(max(C, 128))
+    gs = torch.sigmoid(torch.randn(rows, D, device=dev, generator=g)).to(torch.bfloat16)
+    out = torch.empty(rows, D, device=dev, dtype=torch.bfloat16)
+    sd = (ctypes.c_int * (4 * len(seqs)))(*[x for t in seqs for x in t])
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    flops = sum(4 * S * (S + c) * D + (4 * S * S * D if uncond else 0) for S, c in zip(lens, ctxs))
 
     def launch():
-        rc = L.irtt_attention_async(P(q), P(k), P(v), P(gs), P(ck_), P(cv), None, sd, 2, H, hd, P(out), 1, 2 * S, C, 0)
+        rc = L.irtt_attention_async(P(q), P(k), P(v), P(gs), P(ck_), P(cv), None, sd, len(seqs), H, hd, P(out), 1,
+                                    rows, max(C, 128), 0)
         if rc:
             raise RuntimeError(L.irtt_last_error().decode())
 
@@ -293,7 +312,6 @@ def attn_case(steps):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
-    flops = 4 * S * (S + C) * D + 4 * S * S * D
     return ms, flops / (ms / 1000.0) / 1e12
 
 
@@ -417,8 +435,9 @@ def main():
     ap.add_argument("--codec-only", action="store_true",
                     help="time the config-5 DACVAE decode alone (16 utterances, seeded latents)")
     ap.add_argument("--codec-precision", default="bf16", choices=["bf16", "f32"])
-    ap.add_argument("--attn-case", action="store_true",
-                    help="only the joint attention of one config-3 CFG layer, --steps launches (profiling case)")
+    ap.add_argument("--attn-case", nargs="?", const="c3", default=None, choices=["c3", "c4", "c4p"],
+                    help="only the joint attention of one layer: config-3 CFG step (c3), config-4 CFG step (c4) "
+                         "or config-4 plain step (c4p), --steps launches (profiling case)")
     ap.add_argument("--ckpt", default=None)
     ap.add_argument("--latency-only", action="store_true",
                     help="only the config-3 single-utterance latency (used for profiling runs)")
@@ -433,8 +452,9 @@ def main():
         return codec_only(args)
     if args.attn_case:
         load_pkg()
-        ms, tf = attn_case(args.steps)
-        print(json.dumps({"attn_case_ms": round(ms, 4), "tflops": round(tf, 1)}), flush=True)
+        ms, tf = attn_case(args.steps, args.attn_case)
+        print(json.dumps({"attn_case": args.attn_case, "attn_case_ms": round(ms, 4), "tflops": round(tf, 1)}),
+              flush=True)
         return 0
     if args.gemm_case:
         import torch

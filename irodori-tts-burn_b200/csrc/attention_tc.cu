@@ -1,29 +1,30 @@
 // tcgen05 / TMEM flash attention for sm_100a (hd = 128, bf16 operands).
 //
-// One CTA = one (sequence, head, 128-query tile).  320 threads:
-//   warp 0      TMA producer: per 128-key tile a K tile and a V tile, each on
-//               its own 2-stage ring (self keys first, then context); K runs
-//               two tiles ahead of V
-//   warp 1      TMEM allocator + single-thread MMA issuer, both products with
-//               the A operand in tensor memory so only K and V are read from
-//               shared memory:
-//                 S_j  = Q K_j^T   (A = Q in TMEM, B = K_j K-major)  -> TMEM S[j&1]
+// One CTA = one (sequence, head, 128-query tile); two CTAs share an SM (256
+// TMEM columns and ~98 KB of shared memory each), so one CTA's softmax and
+// load latencies overlap the other's tensor-core work.  192 threads:
+//   warp 0      TMA producer: the Q tile once, then per 64-key tile a K tile
+//               and a V tile, each on its own 2-stage ring (self keys first,
+//               then context); K runs two tiles ahead of V
+//   warp 1      TMEM allocator + single-thread MMA issuer:
+//                 S_j  = Q K_j^T   (A = Q in shared memory, B = K_j, both
+//                                   K-major)                -> TMEM S[j&1]
 //                 O   += P_j V_j   (A = P_j in TMEM, B = V_j MN-major) -> TMEM O
 //               issue order S_0, S_1, then per j: P_j V_j, S_{j+2}; S_{j+2}
 //               overwrites the buffer that held S_j / P_j, which the in-order
-//               tensor pipe has consumed by then
-//   warps 2..9  softmax: thread r of a warp owns query row r of its TMEM lane
-//               quadrant; the two warps of a quadrant split the 128 keys of a
-//               tile (64 each) and exchange row maxima through shared memory.
-//               Per tile a warp loads its 64 scores (one batched wait), takes
-//               the row max on raw scores, writes P = exp2(s*scale - m) as
-//               packed bf16 over its scores' columns (the A operand of P V),
-//               and keeps its half of the row sum.  The running max is only
-//               raised when a row max grows by more than 2^8 (conditional
-//               rescale); then each warp rescales its 64 O columns after the
-//               previous P V has completed.  Skipping is exact: O and l share
-//               the same stale max.
-// TMEM columns: S0 [0,128) S1 [128,256) O [256,384) Q [384,448).
+//               tensor pipe has consumed by then.  A final commit after the
+//               last P V signals the epilogue.
+//   warps 2..5  softmax: thread r of a warp owns query row r of its TMEM lane
+//               quadrant, whole rows, so no cross-warp exchange.  Per tile a
+//               thread loads its 64 scores (one batched wait), takes the row
+//               max, writes P = exp2(s*scale - m) as packed bf16 over the
+//               first 32 columns of the same S buffer (the A operand of P V)
+//               and accumulates the row sum.  The running max is only raised
+//               when a row max grows by more than 2^8 (conditional rescale);
+//               then the warp rescales its rows of O after the previous P V
+//               has completed.  Skipping is exact: O and l share the same
+//               stale max.
+// TMEM columns: S0 [0,64) S1 [64,128) O [128,256).
 // Keys past a sequence's end get -inf scores; a row with no valid key outputs
 // 0.  Output = (O / l) * sigmoid-gate, bf16.
 #include <algorithm>
@@ -40,23 +41,22 @@ namespace {
 
 using namespace tcx;
 
-constexpr int QT = 128, KT = 128, HDIM = 128, THREADS = 320, NKV = 2;
-constexpr uint32_t TILE_BYTES = KT * HDIM * 2;  // 32 KB (two 16 KB 64-column halves)
+constexpr int QT = 128, KT = 64, HDIM = 128, SM_WARPS = 4, THREADS = 64 + 32 * SM_WARPS, NKV = 2;
+constexpr uint32_t Q_BYTES = QT * HDIM * 2;     // 32 KB (two 16 KB 64-column halves)
+constexpr uint32_t Q_HALF = Q_BYTES / 2;
+constexpr uint32_t TILE_BYTES = KT * HDIM * 2;  // 16 KB (two 8 KB 64-column halves)
 constexpr uint32_t HALF = TILE_BYTES / 2;
-// smem: K ring | V ring | exchange | barriers
-constexpr uint32_t OFF_K = 0, OFF_V = NKV * TILE_BYTES;
-constexpr uint32_t OFF_X = OFF_V + NKV * TILE_BYTES;  // [2 slots][2 halves][128 rows] f32 maxima, [2][128] sums
-constexpr uint32_t X_BYTES = (2 * 2 * 128 + 2 * 128) * 4;
-constexpr uint32_t OFF_BAR = OFF_X + X_BYTES;
+// smem: Q | K ring | V ring | barriers
+constexpr uint32_t OFF_Q = 0, OFF_K = Q_BYTES, OFF_V = OFF_K + NKV * TILE_BYTES;
+constexpr uint32_t OFF_BAR = OFF_V + NKV * TILE_BYTES;
 constexpr size_t SMEM = OFF_BAR + 256 + 1024;
-constexpr uint32_t IDESC_S = idesc_bf16(128, 128, false);
-constexpr uint32_t IDESC_O = idesc_bf16(128, 128, true);
-constexpr uint32_t TM_S = 0, TM_O = 256, TM_Q = 384;
+constexpr uint32_t IDESC_S = idesc_bf16(128, KT, false);
+constexpr uint32_t IDESC_O = idesc_bf16(128, HDIM, true);
+constexpr uint32_t TM_S = 0, TM_O = 128, TM_COLS = 256;
 constexpr float RESCALE_LOG2 = 8.f;  // raise the running max only beyond 2^8 growth
 
 struct TcAttnArgs {
   const SeqDesc* seqs;
-  const bf16* q;
   const bf16* gsig;
   bf16* out;
   int H;
@@ -91,10 +91,10 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&t);
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                   const __grid_constant__ CUtensorMap tmCK, const __grid_constant__ CUtensorMap tmCV,
-                   const __grid_constant__ TcAttnArgs a) {
+__global__ void __launch_bounds__(THREADS, 2)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmCK,
+                   const __grid_constant__ CUtensorMap tmCV, const __grid_constant__ TcAttnArgs a) {
   pdl_wait();  // before any read of predecessor output, in every CTA
   pdl_trigger();
   const SeqDesc sd = a.seqs[blockIdx.z];
@@ -106,23 +106,24 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  const uint32_t Q_READY = bar(0), O_DONE = bar(1);
-  auto K_FULL = [&](int s) { return bar(2 + s); };
-  auto K_EMPTY = [&](int s) { return bar(2 + NKV + s); };
-  auto V_FULL = [&](int s) { return bar(2 + 2 * NKV + s); };
-  auto V_EMPTY = [&](int s) { return bar(2 + 3 * NKV + s); };
-  auto S_FULL = [&](int b) { return bar(2 + 4 * NKV + b); };
-  auto P_FULL = [&](int b) { return bar(4 + 4 * NKV + b); };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6 + 4 * NKV);
+  const uint32_t Q_FULL = bar(0), O_DONE = bar(1), O_FINAL = bar(2);
+  auto K_FULL = [&](int s) { return bar(3 + s); };
+  auto K_EMPTY = [&](int s) { return bar(3 + NKV + s); };
+  auto V_FULL = [&](int s) { return bar(3 + 2 * NKV + s); };
+  auto V_EMPTY = [&](int s) { return bar(3 + 3 * NKV + s); };
+  auto S_FULL = [&](int b) { return bar(3 + 4 * NKV + b); };
+  auto P_FULL = [&](int b) { return bar(5 + 4 * NKV + b); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7 + 4 * NKV);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_self = (sd.len + KT - 1) / KT;
   const int n_ctx = (sd.ctx_len + KT - 1) / KT;
-  const int ntiles = n_self + n_ctx;
+  const int ntiles = n_self + n_ctx;  // >= 1: q0 < len
 
   if (threadIdx.x == 0) {
-    mbar_init(Q_READY, 8);
+    mbar_init(Q_FULL, 1);
     mbar_init(O_DONE, 1);
+    mbar_init(O_FINAL, 1);
     for (int r = 0; r < NKV; ++r) {
       mbar_init(K_FULL(r), 1);
       mbar_init(K_EMPTY(r), 1);
@@ -131,15 +132,16 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(S_FULL(b), 1);
-      mbar_init(P_FULL(b), 8);
+      mbar_init(P_FULL(b), SM_WARPS);
     }
     mbar_fence_init();
   }
-  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 512);
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), TM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const uint32_t sQ = smem_u32(sm + OFF_Q);
   auto sK = [&](int s) { return smem_u32(sm + OFF_K + s * TILE_BYTES); };
   auto sV = [&](int s) { return smem_u32(sm + OFF_V + s * TILE_BYTES); };
 
@@ -148,6 +150,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       prefetch_map(&tmK);
       prefetch_map(&tmV);
+      mbar_expect_tx(Q_FULL, Q_BYTES);
+      tma_load_2d(sQ, &tmQ, Q_FULL, h * HDIM, sd.tok_start + q0);
+      tma_load_2d(sQ + Q_HALF, &tmQ, Q_FULL, h * HDIM + 64, sd.tok_start + q0);
+      // the gate tile is only read by the epilogue: start it towards L2 now
+
       auto row_of = [&](int j) { return j < n_self ? sd.tok_start + j * KT : sd.ctx_off + (j - n_self) * KT; };
       auto load_k = [&](int j) {
         const int s = j % NKV;
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tma_load_2d(sV(s) + HALF, m, V_FULL(s), h * HDIM + 64, row_of(j));
       };
       // K two tiles ahead of V, matching the MMA issue order
-      if (ntiles > 0) load_k(0);
+      load_k(0);
       if (ntiles > 1) load_k(1);
       for (int j = 0; j < ntiles; ++j) {
         load_v(j);
@@ -175,8 +182,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0 && ntiles > 0) {
-      mbar_wait(Q_READY, 0);
+    if (lane == 0) {
+      mbar_wait(Q_FULL, 0);
       tc_fence_after();
       auto issue_s = [&](int j) {
         const int r = j % NKV, b = j & 1;
@@ -184,8 +191,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HDIM / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-          umma_ts(tmem + TM_S + b * 128, tmem + TM_Q + kk * 8, sdesc_kmajor(sK(r) + off), IDESC_S, kk != 0);
+          // 16 hd columns: 32 bytes into one of the two 64-column halves
+          const uint64_t da = sdesc_kmajor(sQ + (kk >> 2) * Q_HALF + (kk & 3) * 32);
+          const uint64_t db = sdesc_kmajor(sK(r) + (kk >> 2) * HALF + (kk & 3) * 32);
+          umma_f16(tmem + TM_S + b * KT, da, db, IDESC_S, kk != 0);
         }
         umma_commit(S_FULL(b));
         umma_commit(K_EMPTY(r));
@@ -200,10 +209,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < KT / 16; ++kk) {
           // A = P_j (keys 16kk..16kk+15 packed in 8 columns of S buffer s);
-          // B = V [keys][hd] (MN-major: 64-column halves 16 KB apart, 8-key
+          // B = V [keys][hd] (MN-major: 64-column halves HALF apart, 8-key
           // groups 1 KB apart)
           const uint64_t bdesc = sdesc_sw128(sV(r) + kk * 16 * 128, HALF, 1024);
-          umma_ts(tmem + TM_O, tmem + TM_S + s * 128 + kk * 8, bdesc, IDESC_O, (j | kk) != 0);
+          umma_ts(tmem + TM_O, tmem + TM_S + s * KT + kk * 8, bdesc, IDESC_O, (j | kk) != 0);
         }
         umma_commit(V_EMPTY(r));
         umma_commit(O_DONE);  // one phase per tile
@@ -211,71 +220,41 @@ __global__ void __launch_bounds__(THREADS, 1)
         // pipe executes first
         if (j + 2 < ntiles) issue_s(j + 2);
       }
+      umma_commit(O_FINAL);  // every MMA of this CTA, the last P V included
     }
   } else {
-    // ---------------- softmax warps: two per TMEM lane quadrant ----------------
+    // ---------------- softmax warps: one per TMEM lane quadrant ----------------
     const int quad = warp & 3;
-    const int hh = (warp - 2) >> 2;    // key half of every tile (and hd half of Q / O)
     const int row = quad * 32 + lane;  // query row within the tile
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const int qi = q0 + row;
     const bool row_ok = qi < sd.len;
     const long off = (long)(sd.tok_start + (row_ok ? qi : 0)) * D + h * HDIM;
-    float* xm = reinterpret_cast<float*>(sm + OFF_X);  // [slot][half][row] maxima
-    float* xl = xm + 4 * 128;                          // [half][row] sums
-    auto pair_sync = [&]() {
-      tc_fence_before();
-      asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory");
-      tc_fence_after();
-    };
-    // Q (this warp's 64 hd columns of its rows) -> TMEM, packed bf16 pairs
-    {
-      uint32_t qr[32];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const uint4 v = row_ok ? *reinterpret_cast<const uint4*>(a.q + off + hh * 64 + u * 8) : make_uint4(0, 0, 0, 0);
-        qr[4 * u] = v.x;
-        qr[4 * u + 1] = v.y;
-        qr[4 * u + 2] = v.z;
-        qr[4 * u + 3] = v.w;
-      }
-      tmem_st32(tmem + lane_off + TM_Q + hh * 32, qr);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(Q_READY);
-    }
     float m_run = -INFINITY, l_run = 0.f;
     for (int j = 0; j < ntiles; ++j) {
       const int b = j & 1;
       const int kvalid = (j < n_self ? sd.len - j * KT : sd.ctx_len - (j - n_self) * KT);  // valid keys in tile
-      const int kv_h = kvalid - hh * 64;  // valid keys in this warp's half
       mbar_wait(S_FULL(b), (j >> 1) & 1);
       tc_fence_after();
       uint32_t sr[64];
-      tmem_ld32(tmem + lane_off + TM_S + b * 128 + hh * 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      tmem_ld32(tmem + lane_off + TM_S + b * 128 + hh * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      tmem_ld32(tmem + lane_off + TM_S + b * KT, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_ld32(tmem + lane_off + TM_S + b * KT + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
       tmem_wait_ld();
-      if (kv_h < 64) {
+      if (kvalid < KT) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
-          if (i >= kv_h) sr[i] = __float_as_uint(-INFINITY);
+        for (int i = 0; i < KT; ++i)
+          if (i >= kvalid) sr[i] = __float_as_uint(-INFINITY);
       }
       float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 64; i += 4) {
+      for (int i = 0; i < KT; i += 4) {
         mx0 = fmaxf(mx0, __uint_as_float(sr[i]));
         mx1 = fmaxf(mx1, __uint_as_float(sr[i + 1]));
         mx2 = fmaxf(mx2, __uint_as_float(sr[i + 2]));
         mx3 = fmaxf(mx3, __uint_as_float(sr[i + 3]));
       }
-      // row max of the whole tile: exchange with the other key half.  The
-      // barrier also orders both halves' S loads before the P stores below
-      // (the other half's P overwrites columns this half has just read).
-      xm[(b * 2 + hh) * 128 + row] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-      pair_sync();
-      const float mx = fmaxf(xm[(b * 2) * 128 + row], xm[(b * 2 + 1) * 128 + row]) * a.scale_log2;
-      // conditional rescale of the running max (identical in both halves)
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.scale_log2;
+      // conditional rescale of the running max
       float corr = 1.f;
       const bool raise = mx > m_run + RESCALE_LOG2 || (m_run == -INFINITY && mx > -INFINITY);
       if (raise) {
@@ -283,23 +262,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         m_run = mx;
       }
       const float nbase = m_run == -INFINITY ? 0.f : -m_run;
-      // Rescale this half's O columns (warp-collective) once the previous
-      // P V has completed.
+      // Rescale this warp's rows of O (warp-collective) once the previous
+      // P V has completed: S_j done implies P_{j-2} V_{j-2} done, and
+      // P_j V_j cannot start before this tile's P, so the O_DONE phase in
+      // flight is j-1 or already j.
       if (__any_sync(0xffffffffu, raise) && j > 0) {
         mbar_wait(O_DONE, (j - 1) & 1);
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < HDIM / 32; ++c) {
           uint32_t r[32];
-          tmem_ld32(tmem + lane_off + TM_O + hh * 64 + c * 32, r);
+          tmem_ld32(tmem + lane_off + TM_O + c * 32, r);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
-          tmem_st32(tmem + lane_off + TM_O + hh * 64 + c * 32, r);
+          tmem_st32(tmem + lane_off + TM_O + c * 32, r);
         }
       }
-      // P = 2^(s * scale - m) as packed bf16 over this half's score columns
-      // (keys hh*64 + 2c, +1 in column hh*32 + c of the S buffer)
+      // P = 2^(s * scale - m) as packed bf16: keys 2c, 2c+1 in column c of
+      // the S buffer (this thread's scores are all in registers already)
       uint32_t pk[32];
       float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
@@ -310,7 +291,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         rs1 += p1;
         pk[c] = pack_bf16x2(p0, p1);
       }
-      tmem_st32(tmem + lane_off + TM_S + b * 128 + hh * 32, pk);
+      tmem_st32(tmem + lane_off + TM_S + b * KT, pk);
       tmem_wait_st();
       l_run = l_run * corr + (rs0 + rs1);
       tc_fence_before();
@@ -318,28 +299,23 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive(P_FULL(b));
     }
 
-    // prefetch this row's gate half (independent of the attention result)
-    uint4 gpre[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u)
-      gpre[u] = (a.gsig && row_ok) ? *reinterpret_cast<const uint4*>(a.gsig + off + hh * 64 + u * 8)
-                                   : make_uint4(0, 0, 0, 0);
-    if (ntiles > 0) mbar_wait(O_DONE, (ntiles - 1) & 1);  // last P V
+    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    mbar_wait(O_FINAL, 0);
     tc_fence_after();
-    xl[hh * 128 + row] = l_run;
-    pair_sync();
-    const float lsum = xl[row] + xl[128 + row];
-    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+#pragma unroll 1
+    for (int c = 0; c < HDIM / 32; ++c) {
+      uint4 gv[4];
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
+      for (int u = 0; u < 4; ++u)
+        gv[u] = (a.gsig && row_ok) ? *reinterpret_cast<const uint4*>(a.gsig + off + c * 32 + u * 8)
+                                   : make_uint4(0, 0, 0, 0);
       uint32_t r[32];
-      tmem_ld32(tmem + lane_off + TM_O + hh * 64 + c * 32, r);
+      tmem_ld32(tmem + lane_off + TM_O + c * 32, r);
       tmem_wait_ld();
       if (row_ok) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const uint4 gv = gpre[c * 4 + u];
-          const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gv);
+          const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gv[u]);
           uint32_t op[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
@@ -348,7 +324,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             op[k] = pack_bf16x2(__uint_as_float(r[u * 8 + 2 * k]) * inv * g0,
                                 __uint_as_float(r[u * 8 + 2 * k + 1]) * inv * g1);
           }
-          *reinterpret_cast<uint4*>(a.out + off + hh * 64 + c * 32 + u * 8) = make_uint4(op[0], op[1], op[2], op[3]);
+          *reinterpret_cast<uint4*>(a.out + off + c * 32 + u * 8) = make_uint4(op[0], op[1], op[2], op[3]);
         }
       }
     }
@@ -358,7 +334,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, TM_COLS);
   }
 }
 
@@ -374,7 +350,8 @@ bool attention_tc_supported(const AttnParams& p) {
                        reinterpret_cast<uintptr_t>(p.v) | reinterpret_cast<uintptr_t>(p.out) |
                        (p.gsig ? reinterpret_cast<uintptr_t>(p.gsig) : 0) |
                        (p.ck ? reinterpret_cast<uintptr_t>(p.ck) : 0) | (p.cv ? reinterpret_cast<uintptr_t>(p.cv) : 0);
-  // TMA boxes are 128 rows: keep every tensor at least one box tall
+  // TMA boxes are 128 rows (Q) and 64 rows (K, V, context): keep
+  // every tensor at least one box tall
   const bool ctx_ok = !(p.ck && p.cv) || p.ctx_rows == 0 || p.ctx_rows >= KT;
   return (al & 15) == 0 && p.rows >= QT && ctx_ok;
 }
@@ -389,20 +366,20 @@ void attention_tc(const AttnParams& p, cudaStream_t s) {
   }
   const long D = (long)p.H * HDIM;
   // copies (the map cache may be cleared between calls)
-  const CUtensorMap mk = tma_map_bf16(p.k, p.rows, D, D, 128);
-  const CUtensorMap mv = tma_map_bf16(p.v, p.rows, D, D, 128);
+  const CUtensorMap mq = tma_map_bf16(p.q, p.rows, D, D, QT);
+  const CUtensorMap mk = tma_map_bf16(p.k, p.rows, D, D, KT);
+  const CUtensorMap mv = tma_map_bf16(p.v, p.rows, D, D, KT);
   const bool has_ctx = p.ck && p.cv && p.ctx_rows > 0;
-  const CUtensorMap mck = has_ctx ? tma_map_bf16(p.ck, p.ctx_rows, D, D, 128) : mk;
-  const CUtensorMap mcv = has_ctx ? tma_map_bf16(p.cv, p.ctx_rows, D, D, 128) : mv;
+  const CUtensorMap mck = has_ctx ? tma_map_bf16(p.ck, p.ctx_rows, D, D, KT) : mk;
+  const CUtensorMap mcv = has_ctx ? tma_map_bf16(p.cv, p.ctx_rows, D, D, KT) : mv;
   TcAttnArgs a;
   a.seqs = p.seqs;
-  a.q = reinterpret_cast<const bf16*>(p.q);
   a.gsig = reinterpret_cast<const bf16*>(p.gsig);
   a.out = reinterpret_cast<bf16*>(p.out);
   a.H = p.H;
   a.scale_log2 = p.scale * 1.4426950408889634f;
   dim3 grid((p.max_len + QT - 1) / QT, p.H, p.nseq);
-  launch_pdl(attn_tc_kernel, grid, dim3(THREADS), SMEM, s, mk, mv, mck, mcv, a);
+  launch_pdl(attn_tc_kernel, grid, dim3(THREADS), SMEM, s, mq, mk, mv, mck, mcv, a);
   IRT_CHECK_LAUNCH();
 }
 

@@ -188,13 +188,24 @@ ATTN_PATHS = [(1, 0), (1, 1), (0, 2)]  # (bf16, path): tcgen05, mma.sync, SIMT
 
 
 @pytest.mark.parametrize("bf16,path", ATTN_PATHS)
-@pytest.mark.parametrize("case", ["mixed", "config3"])
+@pytest.mark.parametrize("case", ["mixed", "config3", "ragged"])
 def test_attention_matches_torch(dev, bf16, path, case):
     H, hd = 4, 128
     D = H * hd
     if case == "mixed":  # partial self tiles, empty / tiny / multi-tile contexts
         seqs = [(0, 150, 0, 77), (150, 64, 77, 0), (214, 1, 77, 5), (215, 90, 82, 130)]
         M, nctx = 305, 212
+    elif case == "ragged":  # config-4-like batch: cond rows with contexts, then uncond rows without
+        lens = [37, 129, 300, 64, 65, 255, 3, 191, 385, 128]
+        ctxs = [17, 300, 0, 63, 64, 129, 200, 1, 77, 256]
+        seqs, t, c = [], 0, 0
+        for ln, cl in zip(lens, ctxs):
+            seqs.append((t, ln, c, cl))
+            t, c = t + ln, c + cl
+        for ln in lens:
+            seqs.append((t, ln, 0, 0))
+            t += ln
+        M, nctx = t, c
     else:  # joint-CFG rows of config 3: cond (750 + 576 context keys), uncond (750 keys)
         seqs = [(0, 750, 0, 576), (750, 750, 0, 0)]
         M, nctx = 1500, 576
