@@ -182,6 +182,25 @@ def measured_peaks():
 # Dominant-kernel roofline: the tcgen05 GEMM on this workload's DiT shapes
 # ---------------------------------------------------------------------------
 
+def gemm_layer_bytes(M, D=2048, F=5888):
+    """Algorithmic HBM bytes of the four DiT GEMMs of one layer at M rows:
+    bf16 operands and weights read once, bf16 outputs written once, the f32
+    residual read and written by each of the two residual epilogues."""
+    qkvg = 2 * (M * D + 4 * D * D) + 2 * 4 * M * D
+    wo = 2 * (M * D + D * D) + 2 * 4 * M * D
+    w13 = 2 * (M * D + 2 * F * D) + 2 * M * F
+    w2 = 2 * (M * F + D * F) + 2 * 4 * M * D
+    return qkvg + wo + w13 + w2
+
+
+# DRAM bytes (read + write) of the four DiT GEMMs of one layer per row of M,
+# from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum over the
+# four gemm_kernel launches of `--gemm-case 54504`: 5.751 GB).  The operands
+# and outputs all grow with M (the weights are read about once), so the
+# per-layer traffic at another M is this figure times M.
+GEMM_LAYER_TRAFFIC_PER_ROW = 5750995200 / 54504
+
+
 def gemm_roofline(M, reps=5):
     """Times gemm_kernel (tcgen05) on the four DiT GEMMs of one layer at the
     CFG-step row count M with the same fused epilogues the engine uses, with
@@ -555,7 +574,11 @@ def main():
     peak, hbm, peak_kind = measured_peaks()
     achieved, gemm_ms, gemm_flops = gemm_roofline(2 * ntok)
     roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-            "frac": round(achieved / peak, 4), "traffic": None,
+            "frac": round(achieved / peak, 4),
+            "traffic": round(GEMM_LAYER_TRAFFIC_PER_ROW * 2 * ntok),
+            "traffic_unit": "DRAM bytes per layer (the 4 launches achieved is quoted on)",
+            "algorithmic_bytes": gemm_layer_bytes(2 * ntok),
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 4 launches at M=54504, scaled by M",
             "kernel": "gemm_kernel<256> (tcgen05), 4 DiT GEMMs of one layer at M=%d" % (2 * ntok),
             "peak_kind": f"{peak_kind} burst bf16"}
     sust = measured_sustained()

@@ -10,7 +10,7 @@
 //               two warps per TMEM lane quadrant split the tile's columns (one
 //               128-column head each for QKVG, alternate chunks otherwise)
 // Two TMEM accumulator buffers let the epilogue of tile i overlap the MMAs of
-// tile i+1.  Tiles are walked in grouped order (see tile_coords).  Every
+// tile i+1.  Tiles are walked row-major (see tile_coords).  Every
 // mbarrier wait is bounded by a 4 s watchdog that sets a device error flag
 // instead of hanging.
 #include <cuda.h>
@@ -210,20 +210,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32], int
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Grouped rasterisation: tiles are walked in groups of GROUP_M m-tiles; inside
-// a group n is the outer and m the inner index.  Concurrent CTAs then share a
-// few weight tiles and one group of activation rows (GROUP_M * 128 rows stay
-// L2-resident while every n-tile passes over them), so each operand comes
-// from HBM about once instead of once per n-tile.
-constexpr int GROUP_M = 16;
+// Row-major rasterisation: m is the outer and n the inner tile index, so the
+// CTAs running at one time cover a few row blocks of A and every n-tile of
+// the weight.  Each row block of A then comes from HBM once, and the weight
+// (24-48 MB for the DiT GEMMs), touched by every row block in turn, stays hot
+// in L2.  Measured on the four DiT GEMMs of one layer at M = 54,504: 5.75 GB
+// of DRAM traffic per layer against 7.53 GB for groups of 16 row blocks walked
+// n-outer, and 3 % faster.
 __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& m_idx, int& n_idx) {
-  const int per_group = GROUP_M * n_tiles;
-  const int g = t / per_group;
-  const int r = t - g * per_group;
-  const int first_m = g * GROUP_M;
-  const int gm = min(GROUP_M, m_tiles - first_m);
-  n_idx = r / gm;
-  m_idx = first_m + (r - n_idx * gm);
+  (void)m_tiles;
+  m_idx = t / n_tiles;
+  n_idx = t - m_idx * n_tiles;
 }
 
 template <int N>
