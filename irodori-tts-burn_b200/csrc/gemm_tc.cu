@@ -724,7 +724,9 @@ bool gemm_tc_supported(const EpiParams& p, int K, long lda, long ldb, const void
 
 void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int K, const EpiParams& p,
              cudaStream_t s) {
-  // Tile width: 256 unless 128 fills the last wave clearly better (small M).
+  // Tile width 256 wherever the epilogue allows it.  Narrower tiles fill the
+  // last wave better at small M but re-read A from L2 twice as often, and
+  // measured slower at every M tried (750-54,504 rows).
   // Work slots are SMs (1-CTA tiles of 128 rows) or SM pairs (256 rows).
   const bool pairs = tc::use_pairs(M);
   const int sms = pairs ? tc::num_sms() / 2 : tc::num_sms();
@@ -733,17 +735,25 @@ void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int
   const long t256 = mt * ((N + 255) / 256), t128 = mt * ((N + 127) / 128);
   bool use256 = N >= 256;
   if ((p.mode == EPI_QKVG || p.mode == EPI_CTXKV) && (p.Dq % 256)) use256 = false;
-  if (use256 && tc::wave_eff(t128, sms) > tc::wave_eff(t256, sms) + 0.1) use256 = false;
-  // K-splits for the additive residual epilogue when the tile count leaves
-  // SMs idle: each split keeps >= 8 k-blocks (512 of K).
+  // K-splits for the additive residual epilogue (partial products are
+  // reduce-added into x): the split count that best fills the last wave of
+  // work units, each extra split charged 0.08 of wave efficiency for its
+  // read-modify-write of the residual tile and its shorter main loop; each
+  // split keeps >= 8 k-blocks (512 of K), at most 6 splits.
   int splits = 1;
   const long tiles = use256 ? t256 : t128;
-  if (p.mode == EPI_RESID && !p.row_scale && tiles < sms) {
+  if (p.mode == EPI_RESID && !p.row_scale) {
     const int kb = (K + tc::BK - 1) / tc::BK;
-    splits = (int)std::min<long>((2L * sms) / tiles, kb / 8);
-    if (splits < 1) splits = 1;
-    const int kpb = (kb + splits - 1) / splits;
-    splits = (kb + kpb - 1) / kpb;  // no empty split
+    double best = tc::wave_eff(tiles, sms);
+    for (int sp = 2; sp <= 6 && kb / sp >= 8; ++sp) {
+      const int kpb = (kb + sp - 1) / sp;
+      const int real = (kb + kpb - 1) / kpb;  // no empty split
+      const double score = tc::wave_eff(tiles * real, sms) - 0.08 * (real - 1);
+      if (score > best) {
+        best = score;
+        splits = real;
+      }
+    }
   }
   if (pairs) {
     if (use256) tc::launch<256, 2>(A, lda, B, ldb, M, N, K, splits, p, s);
