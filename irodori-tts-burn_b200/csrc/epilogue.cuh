@@ -244,4 +244,88 @@ __device__ __forceinline__ void epi_head(const EpiParams& p, int m, int n0, cons
   }
 }
 
+// Tensor-core QKVG epilogue with bf16 output staged through shared memory.
+// Lane i of the warp owns row m_base + i and all lanes work on the same head
+// (128 columns starting at n0); the arithmetic is epi_head<128>'s.  Per
+// 64-column half the warp's 32 x 64 bf16 block goes to a 4 KB buffer (16-byte
+// chunks XOR-swizzled by row, so the 32 lanes' writes do not conflict) and is
+// written back as whole 128-byte row segments, four rows per instruction,
+// instead of one 16-byte store per lane into 32 different rows.  Rows at or
+// past M are computed but not stored.
+template <class Acc>
+__device__ __forceinline__ void epi_head_staged(const EpiParams& p, int m_base, int lane, int M, int n0,
+                                                const Acc& acc, uint4* buf) {
+  constexpr int HD = 128;
+  const int Dq = p.Dq;
+  const int which = n0 / Dq;
+  const int col = n0 - which * Dq;
+  const int head = col / HD;
+  bf16* dst = reinterpret_cast<bf16*>(which == 0 ? p.q : which == 1 ? p.k : which == 2 ? p.v : p.g);
+  const float* nw = which == 0 ? p.qn_w + col : which == 1 ? p.kn_w + col : nullptr;
+  const bool rope = which < 2 && head < p.rope_heads;
+  const bool act_sig = which == 3;
+  const int m = m_base + lane;
+  const int mc = m < M ? m : M - 1;  // table lookups stay in bounds for rows past M
+  float inv = 1.f;
+  if (nw) {
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < HD; ++j) { float a = acc(j); ss = fmaf(a, a, ss); }
+    inv = 1.f / sqrtf(ss / (float)HD + p.eps);
+  }
+  const int pos = rope ? (p.tok_pos ? p.tok_pos[mc] : mc) : 0;
+  const float* cs = rope ? p.rope_cos + (long)pos * (HD / 2) : nullptr;
+  const float* sn = rope ? p.rope_sin + (long)pos * (HD / 2) : nullptr;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int j0 = half * 64 + c * 8;
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = acc(j0 + j);
+      if (nw) {
+        const float4 w0 = *reinterpret_cast<const float4*>(nw + j0);
+        const float4 w1 = *reinterpret_cast<const float4*>(nw + j0 + 4);
+        v[0] *= inv * w0.x; v[1] *= inv * w0.y; v[2] *= inv * w0.z; v[3] *= inv * w0.w;
+        v[4] *= inv * w1.x; v[5] *= inv * w1.y; v[6] *= inv * w1.z; v[7] *= inv * w1.w;
+      }
+      if (rope) {
+        const float4 cc4 = *reinterpret_cast<const float4*>(cs + (j0 >> 1));
+        const float4 ss4 = *reinterpret_cast<const float4*>(sn + (j0 >> 1));
+        const float cc[4] = {cc4.x, cc4.y, cc4.z, cc4.w}, sv[4] = {ss4.x, ss4.y, ss4.z, ss4.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float a0 = v[2 * k], a1 = v[2 * k + 1];
+          v[2 * k] = a0 * cc[k] - a1 * sv[k];
+          v[2 * k + 1] = a0 * sv[k] + a1 * cc[k];
+        }
+      }
+      if (act_sig) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __fdividef(1.f, 1.f + __expf(-v[j]));
+      }
+      uint4 u;
+      __nv_bfloat162 t0 = __floats2bfloat162_rn(v[0], v[1]);
+      __nv_bfloat162 t1 = __floats2bfloat162_rn(v[2], v[3]);
+      __nv_bfloat162 t2 = __floats2bfloat162_rn(v[4], v[5]);
+      __nv_bfloat162 t3 = __floats2bfloat162_rn(v[6], v[7]);
+      u.x = *reinterpret_cast<uint32_t*>(&t0);
+      u.y = *reinterpret_cast<uint32_t*>(&t1);
+      u.z = *reinterpret_cast<uint32_t*>(&t2);
+      u.w = *reinterpret_cast<uint32_t*>(&t3);
+      buf[lane * 8 + (c ^ (lane & 7))] = u;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int r = it * 4 + (lane >> 3), ch = lane & 7;
+      const uint4 u = buf[r * 8 + (ch ^ (r & 7))];
+      if (m_base + r < M)
+        *reinterpret_cast<uint4*>(dst + (long)(m_base + r) * Dq + col + half * 64 + ch * 8) = u;
+    }
+    __syncwarp();  // the next half overwrites the buffer
+  }
+}
+
 }  // namespace irt

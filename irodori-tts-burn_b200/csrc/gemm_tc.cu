@@ -409,7 +409,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_ld32(taddr, r2, c + 64);
           tmem_ld32(taddr, r3, c + 96);
           tmem_wait_ld();
-          if (row_ok) epi_head<128>(ep, row, n0 + c, R);
+          if (ep.mode == EPI_QKVG && ep.out_bf16) {
+            // warp-collective: coalesced row segments through this warp's 4 KB buffer
+            const int m_base = m0 + quad * 32;
+            if (m_base < M)
+              epi_head_staged(ep, m_base, lane, M, n0 + c, R,
+                              reinterpret_cast<uint4*>(smem + C::OFF_EPI + (warp - 2) * 4096));
+          } else if (row_ok) {
+            epi_head<128>(ep, row, n0 + c, R);
+          }
         }
       } else if (ep.mode == EPI_SWIGLU) {
 #pragma unroll 1
