@@ -328,4 +328,47 @@ __device__ __forceinline__ void epi_head_staged(const EpiParams& p, int m_base, 
   }
 }
 
+// Tensor-core SWIGLU epilogue with bf16 output staged through shared memory
+// (requires F % 32 == 0).  Lane i owns row m_base + i; all lanes work on the
+// same 64 accumulator columns (32 w1 + 32 w3), i.e. the same 32 outputs.  The
+// warp's 32 x 32 bf16 block goes to a 2 KB buffer (16-byte chunks swizzled by
+// row pair so each 8-lane phase hits distinct banks) and is written back as
+// 64-byte row segments, eight rows per instruction.  Rows at or past M are
+// computed but not stored.
+template <class Acc>
+__device__ __forceinline__ void epi_swiglu_staged(const EpiParams& p, int m_base, int lane, int M, int n0,
+                                                  const Acc& acc, uint4* buf) {
+  constexpr int G = SWIGLU_GROUP;
+  static_assert(G == 32, "staged SWIGLU epilogue assumes 32-column groups");
+  const int f0 = (n0 / (2 * G)) * G;
+  bf16* dst = reinterpret_cast<bf16*>(p.h);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float a = acc(k * 8 + j);
+      v[j] = __fdividef(a, 1.f + __expf(-a)) * acc(G + k * 8 + j);
+    }
+    uint4 u;
+    __nv_bfloat162 t0 = __floats2bfloat162_rn(v[0], v[1]);
+    __nv_bfloat162 t1 = __floats2bfloat162_rn(v[2], v[3]);
+    __nv_bfloat162 t2 = __floats2bfloat162_rn(v[4], v[5]);
+    __nv_bfloat162 t3 = __floats2bfloat162_rn(v[6], v[7]);
+    u.x = *reinterpret_cast<uint32_t*>(&t0);
+    u.y = *reinterpret_cast<uint32_t*>(&t1);
+    u.z = *reinterpret_cast<uint32_t*>(&t2);
+    u.w = *reinterpret_cast<uint32_t*>(&t3);
+    buf[lane * 4 + (k ^ ((lane >> 1) & 3))] = u;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int r = it * 8 + (lane >> 2), k = lane & 3;
+    const uint4 u = buf[r * 4 + (k ^ ((r >> 1) & 3))];
+    if (m_base + r < M) *reinterpret_cast<uint4*>(dst + (long)(m_base + r) * p.F + f0 + k * 8) = u;
+  }
+  __syncwarp();  // the buffer is reused by the warp's next chunk
+}
+
 }  // namespace irt

@@ -429,7 +429,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_ld32(taddr, r0, c);
           tmem_ld32(taddr, r1, c + 32);
           tmem_wait_ld();
-          if (row_ok) epi_chunk_swiglu<Regs<64>, true>(ep, row, n0 + c, R);
+          if (ep.out_bf16 && (ep.F % 32) == 0) {
+            // warp-collective: 64-byte row segments through this warp's buffer
+            const int m_base = m0 + quad * 32;
+            if (m_base < M)
+              epi_swiglu_staged(ep, m_base, lane, M, n0 + c, R,
+                                reinterpret_cast<uint4*>(smem + C::OFF_EPI + (warp - 2) * 4096));
+          } else if (row_ok) {
+            epi_chunk_swiglu<Regs<64>, true>(ep, row, n0 + c, R);
+          }
         }
       } else if (ep.mode == EPI_RESID && ep.x_tma) {
         // Gated residual x += gate * acc without reading x: each 32 x 32 chunk
