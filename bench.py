@@ -476,6 +476,8 @@ def main():
                     help="only the joint attention of one layer: config-3 CFG step (c3), config-4 CFG step (c4) "
                          "or config-4 plain step (c4p), --steps launches (profiling case)")
     ap.add_argument("--ckpt", default=None)
+    ap.add_argument("--shard", type=int, default=0,
+                    help="profiling case: time every rank's config-4 bin of an N-way split on this one GPU")
     ap.add_argument("--latency-only", action="store_true",
                     help="only the config-3 single-utterance latency (used for profiling runs)")
     ap.add_argument("--gemm-case", type=int, default=0,
@@ -485,6 +487,8 @@ def main():
         return reference_arm(args)
     if args.latency_only:
         return latency_only(args)
+    if args.shard:
+        return shard_case(args)
     if args.codec_only:
         return codec_only(args)
     if args.attn_case:
@@ -750,6 +754,55 @@ def codec_only(args):
     print(json.dumps({"codec_decode_ms": round(ms, 3), "precision": args.codec_precision, "frames": frames,
                       "audio_s_per_s": round(frames / FRAME_RATE / (ms / 1000.0), 1),
                       "tflops": round(codec_flops_per_frame() * frames / (ms / 1000.0) / 1e12, 1)}), flush=True)
+    return 0
+
+
+def shard_case(args):
+    """Profiling case for multi-GPU scaling on one GPU: every rank's bin of an
+    N-way split of config 4 (LPT bins on the cost model, exactly as the N-GPU
+    bench assigns them) sampled in turn on this GPU, W warm-up and K timed
+    steps each.  Ranks share nothing on the data path, so a bin's time here is
+    that rank's step time in the N-GPU run, and the N-GPU throughput is the
+    job's audio over the slowest bin's time."""
+    import torch
+    n = int(args.shard)
+    pkg = load_pkg()
+    from irodori_b200 import sharding
+    cfg = model_cfg()
+    ckpt = Path(args.ckpt) if args.ckpt else Path(tempfile.gettempdir()) / "irodori_bench" / "dit_default_l32_s4.safetensors"
+    ensure_checkpoint(ckpt, cfg, 0, 1)
+    params = pkg.SamplerParams(num_steps=40, method="euler",
+                               guidance=pkg.GuidanceConfig(mode="joint", scale_text=3.0, scale_speaker=3.0))
+    eng = pkg.InferenceBuilder(0).load_weights(str(ckpt), precision="bf16").with_sampling(params).build()
+    utts = workload()
+    costs = [sharding.utterance_cost(S, tl, rf) for tl, S, rf, _ in utts]
+    audio_total = sum(u[3] for u in utts)
+    P = cfg["latent_dim"]
+    stream = torch.cuda.Stream()
+    bins = []
+    for r in range(n):
+        mine = sharding.shard_for_rank(costs, r, n)
+        batch = build_batch(utts, mine, P, cfg["text_vocab_size"])
+        keys = ("text_ids", "text_mask", "ref_latent", "ref_mask", "initial_noise")
+        dev_in = {k: batch[k].cuda() for k in keys}
+        out = torch.empty(len(mine), batch["sequence_length"], P, device="cuda")
+        rq = pkg.SamplingRequest(sequence_length=batch["sequence_length"], sequence_lengths=batch["sequence_lengths"],
+                                 **dev_in)
+        for _ in range(args.warmup):
+            eng.sample(rq, out=out, stream=stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            eng.sample(rq, out=out, stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        bins.append({"rank": r, "utterances": len(mine), "latent_frames": sum(utts[i][1] for i in mine),
+                     "audio_seconds": round(sum(utts[i][3] for i in mine), 2), "ms_per_step": round(ms, 2)})
+    worst = max(b["ms_per_step"] for b in bins)
+    print(json.dumps({"shard_case": n, "bins": bins, "slowest_ms": worst,
+                      "projected_value": round(audio_total / (worst / 1000.0), 3), "unit": UNIT}), flush=True)
     return 0
 
 
