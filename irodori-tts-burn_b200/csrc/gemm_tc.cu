@@ -231,6 +231,48 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
   }
 }
 
+// Work decomposition shared by the producer, MMA and epilogue roles.
+//  splits >= 1: units (tile, K-split) dealt round-robin to the work groups
+//    (a group = one CTA, or one CTA pair).
+//  splits < 0 (stream-K; only for the additive RESID epilogue, whose partial
+//    products are reduce-added into x): group g owns the contiguous range
+//    [g * L, (g + 1) * L) of all tiles' k-blocks taken in tile order,
+//    L = ceil(tiles * k_blocks / groups), so every group does the same number
+//    of k-blocks; its units are the pieces of that range inside each tile.
+struct Units {
+  int grp0, ngrp, num_tiles, k_blocks, splits, kpb;
+  long lo, hi;
+  __device__ Units(int g, int ng, int nt, int kb, int sp)
+      : grp0(g), ngrp(ng), num_tiles(nt), k_blocks(kb), splits(sp), kpb(0), lo(0), hi(0) {
+    if (sp > 0) {
+      kpb = (kb + sp - 1) / sp;
+    } else {
+      const long total = (long)nt * kb;
+      const long L = (total + ng - 1) / ng;
+      lo = min(total, (long)g * L);
+      hi = min(total, lo + L);
+    }
+  }
+  // The i-th unit of this group; false once past its last unit.
+  __device__ bool get(int i, int& t, int& kb0, int& kb1) const {
+    if (splits > 0) {
+      const int u = grp0 + i * ngrp;
+      if (u >= num_tiles * splits) return false;
+      t = u / splits;
+      kb0 = (u - t * splits) * kpb;
+      kb1 = min(k_blocks, kb0 + kpb);
+      return true;
+    }
+    if (lo >= hi) return false;
+    t = (int)(lo / k_blocks) + i;
+    const long s = max(lo, (long)t * k_blocks), e = min(hi, (long)(t + 1) * k_blocks);
+    if (s >= e) return false;
+    kb0 = (int)(s - (long)t * k_blocks);
+    kb1 = (int)(e - (long)t * k_blocks);
+    return true;
+  }
+};
+
 template <int N>
 struct Regs {
   uint32_t r[N];
@@ -262,9 +304,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int m_tiles = (M + BMT - 1) / BMT, n_tiles = (N + BN - 1) / BN;
   const int num_tiles = m_tiles * n_tiles;
   const int k_blocks = (K + BK - 1) / BK;
-  // work unit = (tile, K-split); splits > 1 only for the additive RESID epilogue
-  const int kpb = (k_blocks + splits - 1) / splits;
-  const int num_units = num_tiles * splits;
+  // work units: see Units (splits != 1 only for the additive RESID epilogue)
+  const Units units(grp0, ngrp, num_tiles, k_blocks, splits);
 
   auto full = [&](int s) { return smem_u32(&bars[s]); };
   auto empty = [&](int s) { return smem_u32(&bars[STAGES + s]); };
@@ -311,9 +352,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       uint32_t it = 0;
-      for (int u = grp0; u < num_units; u += ngrp) {
-        const int t = u / splits, sp = u - t * splits;
-        const int kb0 = sp * kpb, kb1 = min(k_blocks, kb0 + kpb);
+      int t, kb0, kb1;
+      for (int i = 0; units.get(i, t, kb0, kb1); ++i) {
         int mi_, ni_;
         tile_coords(t, m_tiles, n_tiles, mi_, ni_);
         const int m0 = mi_ * BMT + (int)rank * BM, n0 = ni_ * BN + (int)rank * C::B_ROWS;
@@ -342,9 +382,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- MMA issuer (rank 0 of a pair) ----------------
     if (lane == 0 && rank == 0) {
       uint32_t it = 0, tl = 0;
-      for (int u = grp0; u < num_units; u += ngrp, ++tl) {
-        const int t = u / splits, sp = u - t * splits;
-        const int kb0 = sp * kpb, kb1 = min(k_blocks, kb0 + kpb);
+      int t, kb0, kb1;
+      for (int i = 0; units.get(i, t, kb0, kb1); ++i, ++tl) {
         const int buf = tl & 1;
         const uint32_t aph = (tl >> 1) & 1;
         mbar_wait(tempty(buf), aph ^ 1);
@@ -383,8 +422,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     // rank 0's accumulator-empty barriers, addressed through the cluster window
     const uint32_t te0 = CG == 2 ? map_rank0(tempty(0)) : tempty(0);
     const uint32_t te1 = CG == 2 ? map_rank0(tempty(1)) : tempty(1);
-    for (int u = grp0; u < num_units; u += ngrp, ++tl) {
-      const int t = u / splits;
+    int t, kb0, kb1;
+    for (int i = 0; units.get(i, t, kb0, kb1); ++i, ++tl) {
       const int buf = tl & 1;
       const uint32_t aph = (tl >> 1) & 1;
       int mi_, ni_;
@@ -497,7 +536,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const float g = (ep.gate && col_ok) ? ep.gate[n] : 1.f;
           const int r0 = m0 + quad * 32;
           float* xc = ep.x + n;
-          if (splits > 1) {
+          if (splits != 1) {  // K-split or stream-K partial products: atomic adds
 #pragma unroll 8
             for (int i = 0; i < 32; ++i)
               if (col_ok && r0 + i < M) atomicAdd(xc + (long)(r0 + i) * N, g * stg[i * 33 + lane]);
@@ -681,7 +720,8 @@ void launch(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int 
   const CUtensorMap tx = xtma ? tensor_map_resid(p.x, M, N, N) : ta;
   EpiParams pp = p;
   pp.x_tma = xtma ? 1 : 0;
-  const int units = ((M + BM * CG - 1) / (BM * CG)) * ((N + BN - 1) / BN) * splits;
+  // stream-K (splits < 0) spreads the k-blocks over every available group
+  const int units = splits < 0 ? (1 << 30) : ((M + BM * CG - 1) / (BM * CG)) * ((N + BN - 1) / BN) * splits;
   if constexpr (CG == 1) {
     const int grid = units < num_sms() ? units : num_sms();
     launch_pdl(gemm_kernel<BN, 1>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, tx, M, N, K, splits, pp);
@@ -755,12 +795,17 @@ void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int
   // reduce-added into x): the split count that best fills the last wave of
   // work units, each extra split charged 0.08 of wave efficiency for its
   // read-modify-write of the residual tile and its shorter main loop; each
-  // split keeps >= 8 k-blocks (512 of K), at most 6 splits.
+  // split keeps >= 8 k-blocks (512 of K), at most 6 splits.  When no split
+  // pays but the last wave is still poorly filled and K is long (>= 64
+  // k-blocks, so a group's span crosses few tile boundaries), the GEMM runs
+  // stream-K instead (splits = -1, see Units).  Measured: stream-K is +9 % on
+  // W2 at 3,400 rows and slower than the split rule wherever that one splits.
   int splits = 1;
   const long tiles = use256 ? t256 : t128;
   if (p.mode == EPI_RESID && !p.row_scale) {
     const int kb = (K + tc::BK - 1) / tc::BK;
-    double best = tc::wave_eff(tiles, sms);
+    const double eff1 = tc::wave_eff(tiles, sms);
+    double best = eff1;
     for (int sp = 2; sp <= 6 && kb / sp >= 8; ++sp) {
       const int kpb = (kb + sp - 1) / sp;
       const int real = (kb + kpb - 1) / kpb;  // no empty split
@@ -770,6 +815,7 @@ void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int
         splits = real;
       }
     }
+    if (splits == 1 && eff1 < 0.8 && kb >= 64 && tiles * kb >= 8L * sms) splits = -1;
   }
   if (pairs) {
     if (use256) tc::launch<256, 2>(A, lda, B, ldb, M, N, K, splits, p, s);

@@ -147,10 +147,13 @@ def test_gemm_swiglu_and_resid(dev, path):
     assert err < 1e-4, f"resid rel err {err}"
 
 
-@pytest.mark.parametrize("M,N,K", [(300, 2048, 5888), (750, 2048, 2048), (1500, 2048, 5888)])
+@pytest.mark.parametrize("M,N,K", [(300, 2048, 5888), (750, 2048, 2048), (1500, 2048, 5888), (3000, 2048, 5888),
+                                   (3400, 2048, 5888)])
 def test_gemm_resid_split_k(dev, M, N, K):
-    """Few tiles -> the residual GEMM runs K-split with vector atomics; the
-    result must equal x + gate * (A @ W^T) (order-independent to fp32 rounding)."""
+    """Few tiles -> the residual GEMM reduce-adds partial products: K-splits
+    (M = 300-3000) or stream-K (M = 3400, K = 5888: each SM pair takes an equal
+    span of all tiles' k-blocks, spans crossing tile boundaries); the result
+    must equal x + gate * (A @ W^T) (order-independent to fp32 rounding)."""
     g = torch.Generator(device=dev).manual_seed(M + K)
     A = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
     W = (torch.randn(N, K, device=dev, generator=g) * 0.05).to(torch.bfloat16)
