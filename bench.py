@@ -293,6 +293,42 @@ def gemm_roofline(M, reps=5, sustain_s=0.0):
 # CPU leg: the oracle (restatement of the reference path) on the host cores
 # ---------------------------------------------------------------------------
 
+def row_case(M, steps):
+    """Profiling case: the adaLN modulate row kernel (rownorm_reg_kernel, the
+    bandwidth-bound kernel of each DiT block) at M rows of D = 2048: f32 x in,
+    bf16 h out, CUDA events over `steps` back-to-back launches.  At the
+    config-4 CFG step (M = 54,504) x alone is 446 MB, larger than L2.
+    Returns (us per launch, algorithmic GB/s)."""
+    import torch
+    L = ctypes.CDLL(str(PKG_DIR / "libirodori_b200_testhooks.so"))
+    L.irtt_adaln_modulate.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 3 + [ctypes.c_float]
+    L.irtt_last_error.restype = ctypes.c_char_p
+    D = 2048
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(M, D, device="cuda", generator=g)
+    shift = torch.randn(D, device="cuda", generator=g) * 0.1
+    scale = torch.randn(D, device="cuda", generator=g) * 0.1
+    h = torch.empty(M, D, device="cuda", dtype=torch.bfloat16)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def launch():
+        if L.irtt_adaln_modulate(P(x), P(shift), P(scale), P(h), 1, M, D, 1e-5):
+            raise RuntimeError(L.irtt_last_error().decode())
+
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        launch()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / steps
+    nbytes = M * D * 4 + M * D * 2 + 2 * D * 4
+    return us, nbytes / (us * 1e-6) / 1e9
+
+
 def attn_case(steps, which="c3"):
     """Profiling case: the joint attention of one DiT layer, H = 16, hd = 128,
     bf16, through the tcgen05 kernel; `steps` launches timed with CUDA events.
@@ -476,6 +512,8 @@ def main():
                     help="only the joint attention of one layer: config-3 CFG step (c3), config-4 CFG step (c4) "
                          "or config-4 plain step (c4p), --steps launches (profiling case)")
     ap.add_argument("--ckpt", default=None)
+    ap.add_argument("--row-case", type=int, default=0,
+                    help="profiling case: the adaLN modulate row kernel alone at M rows, --steps launches")
     ap.add_argument("--shard", type=int, default=0,
                     help="profiling case: time every rank's config-4 bin of an N-way split on this one GPU")
     ap.add_argument("--latency-only", action="store_true",
@@ -489,6 +527,13 @@ def main():
         return latency_only(args)
     if args.shard:
         return shard_case(args)
+    if args.row_case:
+        load_pkg()
+        us, gbs = row_case(args.row_case, args.steps)
+        peak = measured_peaks()[1]
+        print(json.dumps({"row_case_M": args.row_case, "us_per_launch": round(us, 2), "gbs": round(gbs, 1),
+                          "hbm_peak_gbs": peak, "frac": round(gbs / peak, 4)}), flush=True)
+        return 0
     if args.codec_only:
         return codec_only(args)
     if args.attn_case:

@@ -156,6 +156,14 @@ IRTT_API int irtt_sync_check() {
   });
 }
 
+// adaLN modulate rows (ops.cu): h = x / sqrt(mean(x^2) + eps) * (1 + scale) +
+// shift, f32 in, bf16 or f32 out; device pointers, asynchronous (check with
+// irtt_sync_check()).
+IRTT_API int irtt_adaln_modulate(const float* x, const float* shift, const float* scale, void* h, int out_bf16, int M,
+                                 int D, float eps) {
+  return guard([&] { irt::adaln_modulate(x, shift, scale, h, out_bf16, M, D, eps, nullptr); });
+}
+
 // One implicit-GEMM convolution of the bf16 codec path (conv_tc.cu); all
 // pointers are device memory, w packed [phases][cout][taps][cin_pad] bf16.
 IRTT_API int irtt_conv_tc(const void* in, int rows_in, int cin, const void* w, int cin_pad, int taps, int phases,

@@ -166,6 +166,24 @@ def test_gemm_resid_split_k(dev, M, N, K):
     assert err < 1e-5, f"split-K resid rel err {err}"
 
 
+@pytest.mark.parametrize("out_bf16", [1, 0])
+def test_adaln_modulate_matches_torch(dev, out_bf16):
+    """adaLN modulate rows (the LowRankAdaLn output, h = x / sqrt(mean(x^2) +
+    eps) * (1 + scale) + shift), f32 in, bf16 or f32 out, against torch fp32."""
+    M, D, eps = 300, 2048, 1e-5
+    g = torch.Generator(device=dev).manual_seed(21)
+    x = torch.randn(M, D, device=dev, generator=g) * 3
+    shift = torch.randn(D, device=dev, generator=g) * 0.1
+    scale = torch.randn(D, device=dev, generator=g) * 0.1
+    h = torch.full((M, D), float("nan"), device=dev).to(torch.bfloat16 if out_bf16 else torch.float32)
+    L = hooks()
+    L.irtt_adaln_modulate.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 3 + [ctypes.c_float]
+    check(L.irtt_adaln_modulate(ptr(x), ptr(shift), ptr(scale), ptr(h), out_bf16, M, D, eps))
+    ref = x / torch.sqrt((x * x).mean(-1, keepdim=True) + eps) * (1 + scale) + shift
+    err = (h.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < (1e-2 if out_bf16 else 1e-5), f"adaln rel err {err}"
+
+
 def _attn_ref(q, k, v, g, ck, cv, key_mask, seqs, H, hd):
     out = torch.zeros_like(q, dtype=torch.float32)
     for (ts, ln, co, cl) in seqs:
