@@ -455,6 +455,15 @@ def job_flops(utts, min_t=0.5, steps=40):
     return tot
 
 
+def config4_dict(audio_total, world):
+    """The `config` object of both arms' JSON line (config 4 at N GPUs)."""
+    return {"workload": "config4: 64 utterances (text 16-256, 2-30 s, speaker 5-15 s), 40-step Euler, "
+                        "joint CFG 3.0, min_t 0.5, ragged batches, LPT bins per rank",
+            "utterances": N_UTT, "audio_seconds": round(audio_total, 2), "model_dim": 2048,
+            "layers": 24, "latent_dim": 32, "parallelism": f"utterance shards x{world}",
+            "l2": "weights (4.6 GB bf16) exceed L2; no flush needed"}
+
+
 def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -472,8 +481,7 @@ def reference_arm(args):
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config4: 64 utterances, 40-step joint CFG (bounded CPU sample)",
-                       "utterances": N_UTT},
+            "config": config4_dict(audio, args.gpus),
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -674,11 +682,7 @@ def main():
     line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 2), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights and inputs)",
-            "config": {"workload": "config4: 64 utterances (text 16-256, 2-30 s, speaker 5-15 s), 40-step Euler, "
-                                   "joint CFG 3.0, min_t 0.5, ragged batches, LPT bins per rank",
-                       "utterances": N_UTT, "audio_seconds": round(audio_total, 2), "model_dim": 2048,
-                       "layers": 24, "latent_dim": 32, "parallelism": f"utterance shards x{world}",
-                       "l2": "weights (4.6 GB bf16) exceed L2; no flush needed"},
+            "config": config4_dict(audio_total, world),
             "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
