@@ -188,3 +188,83 @@ def test_codec_decode_shapes_and_bounds(oracle, synth, tmp_path):
     wav = oracle.codec_decode(W, torch.randn(2, 3, 32))
     assert wav.shape == (2, 1, 3 * 1920)
     assert wav.abs().max() <= 1.0
+
+
+def test_temporal_score_rescale_kats(oracle):
+    # src/rf/math.rs tests: no-op at t >= 1 (exact), identity when sigma = 0 or k = 1,
+    # finite output, and the hand-computed value 4/3 at t = 0.5, k = 2, sigma = 1
+    v = torch.tensor([[[1.0, 2.0]]])
+    assert torch.equal(oracle.temporal_score_rescale(v, torch.tensor([[[5.0, 6.0]]]), 1.0, 1.5, 0.5), v)
+    v = torch.tensor([[[3.0, 4.0]]])
+    assert torch.equal(oracle.temporal_score_rescale(v, torch.tensor([[[9.0, 10.0]]]), 1.5, 2.0, 1.0), v)
+    v = torch.tensor([[[2.0, 3.0]]])
+    r = oracle.temporal_score_rescale(v, torch.tensor([[[1.0, 1.0]]]), 0.5, 1.0, 0.0)
+    assert (r - v).abs().max().item() < 1e-5
+    v = torch.tensor([[[2.0, -1.0]]])
+    r = oracle.temporal_score_rescale(v, torch.tensor([[[0.5, 0.3]]]), 0.4, 1.0, 2.5)
+    assert (r - v).abs().max().item() < 1e-5
+    r = oracle.temporal_score_rescale(torch.tensor([[[1.0, -1.0]]]), torch.tensor([[[0.5, 0.3]]]), 0.3, 2.0, 1.0)
+    assert torch.isfinite(r).all()
+    r = oracle.temporal_score_rescale(torch.tensor([[[1.0]]]), torch.tensor([[[0.0]]]), 0.5, 2.0, 1.0)
+    assert abs(r.item() - 4.0 / 3.0) < 1e-5
+
+
+def _unit_cache(oracle, seq_text, seq_aux, heads, hd):
+    ones = lambda s: torch.ones(1, s, heads, hd)  # noqa: E731
+    return oracle.KvCache(ones(seq_text), ones(seq_text), ones(seq_aux), ones(seq_aux),
+                          torch.ones(1, seq_text + seq_aux, dtype=torch.bool))
+
+
+def test_scale_speaker_kv_cache_kats(oracle):
+    # src/rf/kv_scaling.rs tests: scaling by 2 doubles the speaker (aux) K/V, leaves the
+    # text K/V alone and rebuilds the joint context [text | aux] from them
+    (c,) = oracle.scale_speaker_kv_cache([_unit_cache(oracle, 4, 3, 2, 8)], 2.0, None)
+    assert torch.equal(c.aux_k, torch.full_like(c.aux_k, 2.0)) and torch.equal(c.aux_v, torch.full_like(c.aux_v, 2.0))
+    assert torch.equal(c.text_k, torch.ones_like(c.text_k))
+    ctx = c.ctx_k.reshape(-1)
+    n_text = 4 * 2 * 8
+    assert torch.equal(ctx[:n_text], torch.ones(n_text)) and torch.equal(ctx[n_text:], torch.full((3 * 2 * 8,), 2.0))
+    # max_layers = 1 scales only the first layer's cache
+    s = oracle.scale_speaker_kv_cache([_unit_cache(oracle, 2, 2, 1, 4), _unit_cache(oracle, 2, 2, 1, 4)], 3.0, 1)
+    assert s[0].aux_k.max().item() == 3.0 and s[1].aux_k.max().item() == 1.0
+
+
+def test_low_rank_adaln_zero_init_gate_is_tanh(oracle, synth):
+    # src/model/norm.rs low_rank_adaln_zero_init_gate_is_tanh_of_input: with zero-initialised
+    # up projections the gate is tanh of the raw gate input (0.5 -> tanh(0.5))
+    import json
+    D, r = 16, 4
+    g = torch.Generator().manual_seed(0)
+    t = {}
+    for k in ("shift", "scale", "gate"):
+        t[f"a.{k}_down.weight"] = torch.randn(r, D, generator=g)
+        t[f"a.{k}_up.weight"] = torch.zeros(D, r)
+    W = oracle.Weights(t, json.dumps(synth.TINY_CONFIG))
+    h, gate = oracle.low_rank_adaln(W, "a", torch.ones(1, 3, D), torch.full((1, 1, 3 * D), 0.5), 1e-6)
+    assert gate.shape == (1, 1, D) and h.shape == (1, 3, D)
+    assert (gate - math.tanh(0.5)).abs().max().item() < 1e-5
+
+
+def test_hidden_dim_rule(oracle, synth):
+    # src/model/diffusion.rs hidden_dim_calculation: ((model_dim as f64 * mlp_ratio) as usize).max(1)
+    import json
+    for dim, ratio in ((32, 2.0), (2048, 2.875), (16, 2.7), (4, 0.1)):
+        c = dict(synth.TINY_CONFIG, model_dim=dim, mlp_ratio=ratio)
+        assert oracle.ModelConfig.from_json(json.dumps(c)).hidden_dim() == max(int(dim * ratio), 1)
+
+
+def test_forward_with_zero_inputs_is_finite(oracle, synth, tmp_path):
+    # src/model/diffusion.rs block_residual_connection_with_zeros: zero latents and a zero
+    # condition give finite outputs (safe norms, safe softmax)
+    p = tmp_path / "z.safetensors"
+    synth.make_dit_checkpoint(str(p), synth.TINY_CONFIG, seed=0, init="full")
+    W = oracle.Weights.load(str(p))
+    r = synth.make_request(synth.TINY_CONFIG, 1, 2, 3, 4, seed=1)
+    req = oracle.SamplingRequest(text_ids=r["text_ids"], text_mask=r["text_mask"], sequence_length=4,
+                                 ref_latent=torch.zeros_like(r["ref_latent"]), ref_mask=r["ref_mask"],
+                                 initial_noise=torch.zeros_like(r["initial_noise"]))
+    cond = oracle.encode_conditions(W, req)
+    cos, sin = oracle.rope_tables(W.cfg.head_dim(), 4)
+    out = oracle.dit_forward(W, torch.zeros_like(r["initial_noise"]), torch.zeros(1), oracle.build_kv_caches(W, cond),
+                             cos, sin)
+    assert torch.isfinite(out).all()
