@@ -199,6 +199,19 @@ class SpeakerKvConfig:
     min_t: Optional[float] = None
 
 
+def _rs_f32(x: float) -> str:
+    """An f32 formatted the way Rust's `Display` does (shortest decimal that
+    round-trips the f32, no exponent, integral values without a fraction,
+    `NaN` / `inf` / `-inf`): the reference's error messages print f32 fields
+    this way."""
+    import numpy as np
+    if math.isnan(x):
+        return "NaN"
+    if math.isinf(x):
+        return "inf" if x > 0 else "-inf"
+    return np.format_float_positional(np.float32(x), unique=True, trim="-")
+
+
 @dataclass
 class SamplerParams:
     """src/rf/params.rs:61-92."""
@@ -219,13 +232,14 @@ class SamplerParams:
                         ("guidance.scale_caption", g.scale_caption),
                         ("guidance.scale_speaker", g.scale_speaker)):
             if not math.isfinite(s):
-                raise ValueError(f"{name} must be finite, got {s}")
+                raise ValueError(f"{name} must be finite, got {_rs_f32(s)}")
         if not math.isfinite(g.min_t) or not (0.0 <= g.min_t <= 1.0):
-            raise ValueError(f"guidance.min_t must be finite and in [0, 1], got {g.min_t}")
+            raise ValueError(f"guidance.min_t must be finite and in [0, 1], got {_rs_f32(g.min_t)}")
         if not math.isfinite(g.max_t) or not (0.0 <= g.max_t <= 1.0):
-            raise ValueError(f"guidance.max_t must be finite and in [0, 1], got {g.max_t}")
+            raise ValueError(f"guidance.max_t must be finite and in [0, 1], got {_rs_f32(g.max_t)}")
         if g.min_t > g.max_t:
-            raise ValueError(f"guidance.min_t ({g.min_t}) must not exceed guidance.max_t ({g.max_t})")
+            raise ValueError(f"guidance.min_t ({_rs_f32(g.min_t)}) must not exceed guidance.max_t "
+                             f"({_rs_f32(g.max_t)})")
         if self.truncation_factor is not None and (
                 self.truncation_factor <= 0.0 or not math.isfinite(self.truncation_factor)):
             raise ValueError("truncation_factor must be finite and > 0")

@@ -73,6 +73,21 @@ def test_validate_messages_through_c_abi(pkg, kw, msg):
     assert ei.value.kind == "Config"
 
 
+@pytest.mark.parametrize("g", [dict(scale_text=float("nan")), dict(scale_speaker=float("-inf")), dict(min_t=2.0),
+                               dict(min_t=-0.25), dict(max_t=1.0000001), dict(min_t=0.9, max_t=0.1),
+                               dict(min_t=float("nan"))])
+def test_validate_messages_match_oracle(pkg, oracle, g):
+    """The C ABI and the oracle reject the same guidance values with the same
+    text, f32 fields printed the way the reference's Rust formats them."""
+    if not pkg.LIB_PATH.exists():
+        pytest.skip("library not built")
+    with pytest.raises(pkg.ConfigError) as ec:
+        pkg.SamplerParams(guidance=pkg.GuidanceConfig(**g)).validate()
+    with pytest.raises(ValueError) as eo:
+        oracle.SamplerParams(guidance=oracle.GuidanceConfig(**g)).validate()
+    assert str(ec.value).endswith(str(eo.value)), (str(ec.value), str(eo.value))
+
+
 def test_unknown_method_is_unsupported_mode(pkg):
     if not pkg.LIB_PATH.exists():
         pytest.skip("library not built")

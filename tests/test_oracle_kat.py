@@ -136,13 +136,27 @@ def test_snake_and_pads(oracle):
     (dict(min_t=0.8, max_t=0.6), "guidance.min_t (0.8) must not exceed guidance.max_t (0.6)"),
     (dict(truncation_factor=0.0), "truncation_factor must be finite and > 0"),
     (dict(method="plms4", mode="alternating"), "PLMS4 is not compatible"),
+    (dict(max_t=1.5), "guidance.max_t must be finite and in [0, 1], got 1.5"),
+    (dict(scale_text=float("nan")), "guidance.scale_text must be finite, got NaN"),
+    (dict(min_t=2.0), "guidance.min_t must be finite and in [0, 1], got 2"),
+    (dict(scale_speaker=float("inf")), "guidance.scale_speaker must be finite, got inf"),
+    (dict(temporal_rescale=(float("nan"), 1.0)), "temporal_rescale.k must be finite"),
+    (dict(temporal_rescale=(1.0, 0.0)), "temporal_rescale.sigma must not be zero"),
+    (dict(speaker_kv=(0.0, None)), "speaker_kv.scale must be finite and > 0"),
+    (dict(speaker_kv=(-1.0, None)), "speaker_kv.scale must be finite and > 0"),
+    (dict(speaker_kv=(float("inf"), None)), "speaker_kv.scale must be finite and > 0"),
+    (dict(speaker_kv=(1.5, 1.5)), "speaker_kv.min_t must be finite and in [0, 1]"),
 ])
 def test_params_validate_rejections(oracle, bad, msg):
     # src/rf/params.rs:253-378
     g = oracle.GuidanceConfig(mode=bad.get("mode", "independent"), min_t=bad.get("min_t", 0.5),
-                              max_t=bad.get("max_t", 1.0))
+                              max_t=bad.get("max_t", 1.0), scale_text=bad.get("scale_text", 3.0),
+                              scale_speaker=bad.get("scale_speaker", 5.0))
+    skv = bad.get("speaker_kv")
     p = oracle.SamplerParams(num_steps=bad.get("num_steps", 40), method=bad.get("method", "euler"), guidance=g,
-                             truncation_factor=bad.get("truncation_factor"))
+                             truncation_factor=bad.get("truncation_factor"),
+                             temporal_rescale=bad.get("temporal_rescale"),
+                             speaker_kv=None if skv is None else oracle.SpeakerKvConfig(scale=skv[0], min_t=skv[1]))
     with pytest.raises(ValueError) as ei:
         p.validate()
     assert msg in str(ei.value)
