@@ -8,6 +8,8 @@
 #include "common.hpp"
 #include "engine.hpp"
 #include "kernels.hpp"
+#include "lora.hpp"
+#include "safetensors.hpp"
 
 #define IRTT_API extern "C" __attribute__((visibility("default")))
 
@@ -143,6 +145,22 @@ IRTT_API int irtt_attention_async(const void* q, const void* k, const void* v, c
     p.path = path;
     if (path == 0 && bf16_io && !irt::attention_tc_supported(p)) throw irt::Error(4, "tcgen05 attention unsupported");
     irt::attention(p, bf16_io, nullptr);
+  });
+}
+
+// PEFT LoRA merge on the host (lora.hpp: the routine the engine runs when it
+// loads base + adapter): tensor `name` of the merged checkpoint decoded to f32
+// into out (n values), and the number of merged tensors in *merged.  Needs no
+// GPU.
+IRTT_API int irtt_lora_merged_tensor(const char* base_path, const char* adapter_dir, const char* name, float* out,
+                                     long n, int* merged) {
+  return guard([&] {
+    irt::SafeTensorsFile st(base_path);
+    const std::vector<std::string> m = irt::apply_lora(st, adapter_dir);
+    const irt::TensorView& v = st.get(name);
+    if ((long)v.numel() != n) throw irt::Error(IRT_E_INVALID_ARG, "size mismatch for " + std::string(name));
+    irt::decode_to_f32(v, out);
+    if (merged) *merged = (int)m.size();
   });
 }
 
