@@ -282,3 +282,37 @@ def test_forward_with_zero_inputs_is_finite(oracle, synth, tmp_path):
     out = oracle.dit_forward(W, torch.zeros_like(r["initial_noise"]), torch.zeros(1), oracle.build_kv_caches(W, cond),
                              cos, sin)
     assert torch.isfinite(out).all()
+
+
+def test_encoders_zero_masked_positions_and_survive_all_masked(oracle, synth, tmp_path):
+    # src/model/text_encoder.rs text_encoder_masked_positions_are_zero /
+    # text_encoder_all_false_mask_no_nan; src/model/speaker_encoder.rs
+    # speaker_encoder_masked_positions_are_zero
+    p = tmp_path / "e.safetensors"
+    synth.make_dit_checkpoint(str(p), synth.TINY_CONFIG, seed=0, init="full")
+    W = oracle.Weights.load(str(p))
+    c, eps = W.cfg, W.cfg.norm_eps
+    ids = torch.zeros(1, 4, dtype=torch.long)
+    out = oracle.text_encoder(W, "text_encoder", ids, torch.tensor([[True, True, False, False]]), c.text_layers,
+                              c.text_heads, eps)
+    assert out[:, 2:].abs().sum().item() == 0.0 and out[:, :2].abs().sum().item() > 0
+    out = oracle.text_encoder(W, "text_encoder", ids, torch.zeros(1, 4, dtype=torch.bool), c.text_layers,
+                              c.text_heads, eps)
+    assert torch.isfinite(out).all()
+    lat = torch.ones(1, 4, W["speaker_encoder.in_proj.weight"].shape[1])
+    out = oracle.speaker_encoder(W, "speaker_encoder", lat, torch.tensor([[True, True, False, False]]),
+                                 c.speaker_layers, c.speaker_heads, eps)
+    assert out[:, 2:].abs().sum().item() == 0.0
+
+
+def test_speaker_patching(oracle):
+    # src/model/speaker_encoder.rs patch_halves_length_doubles_dim, patch_mask_false_propagates,
+    # patch_noop_when_size_1, patch_too_short_returns_error
+    s, m = oracle.patch_sequence_with_mask(torch.ones(2, 8, 4), torch.ones(2, 8, dtype=torch.bool), 2)
+    assert s.shape == (2, 4, 8) and m.shape == (2, 4)
+    _, m = oracle.patch_sequence_with_mask(torch.ones(1, 4, 2), torch.tensor([[True, True, True, False]]), 2)
+    assert m.tolist() == [[True, False]]
+    s, m = oracle.patch_sequence_with_mask(torch.ones(1, 5, 3), torch.ones(1, 5, dtype=torch.bool), 1)
+    assert s.shape == (1, 5, 3) and m.shape == (1, 5)
+    with pytest.raises(ValueError, match="too short"):
+        oracle.patch_sequence_with_mask(torch.ones(1, 1, 4), torch.ones(1, 1, dtype=torch.bool), 2)
