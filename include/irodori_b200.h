@@ -222,14 +222,19 @@ IRT_API int irt_codec_decode_ragged(irt_codec* c, const float* latent, int32_t b
  * by every GPU that loads it until exit), so the call allocates nothing.
  * It always runs the fp32 SIMT decoder, whatever the codec's precision.
  *   - latent [batch, frames, 32] and wav [batch, 1, frames * hop] must be
- *     device (or managed) memory; the call returns once wav is complete.
+ *     device memory of the codec's own GPU (or managed memory): the kernels
+ *     read and write them in place.  Anything else fails with
+ *     IRT_E_INVALID_ARG.  The call returns once wav is complete.
  *   - Capacity: batch * frames <= 7 latent frames (280 ms) for the full-width
  *     DACVAE; larger requests fail with IRT_E_SHAPE and run nothing.
  *   - The array is shared by every call on a device and keeps the last call's
  *     contents (nothing in it needs to start at zero); calls that overlap on the
  *     GPU race and must be serialised by the caller.
- *   - The first call on a device resolves the array's address; make it before
- *     any stream capture.
+ *   - irt_codec_create resolves the array's device address on its GPU (under
+ *     lazy module loading, the moment the array is placed on that GPU); if
+ *     that failed, the first call retries it and reports the failure.
+ *   - Every call ends by synchronising its stream, so it cannot be recorded
+ *     into a CUDA graph by stream capture.
  */
 IRT_API int irt_codec_decode_noalloc(irt_codec* c, const float* latent, int32_t batch, int32_t frames, float* wav,
                                      void* stream);

@@ -287,6 +287,30 @@ def _as_buffer(x, dtype: str, keep: list):
     return a.ctypes.data, a.shape, False
 
 
+def _stream_arg(stream, device: int, on_device: bool, owner):
+    """Stream handle for one C call.
+
+    An explicit ``stream`` (a torch stream or a raw ``cudaStream_t`` as an int)
+    is used as is.  Without one, a call that reads or writes CUDA tensors runs
+    on a side stream of ``owner`` (one per engine or codec) that first waits
+    for torch's current stream on ``device``: work torch has queued on those
+    tensors (their creation, a previous kernel) completes before the engine
+    reads them.  The C calls return only after their own work is complete, so
+    nothing has to be ordered on the way back.  Host-only calls pass NULL (the
+    library's own stream)."""
+    if stream is not None:
+        return ctypes.c_void_p(stream if isinstance(stream, int) else stream.cuda_stream)
+    if not on_device:
+        return None
+    import torch
+    side = getattr(owner, "_side_stream", None)
+    if side is None:
+        side = torch.cuda.Stream(device=device)
+        owner._side_stream = side
+    side.wait_stream(torch.cuda.current_stream(device))
+    return ctypes.c_void_p(side.cuda_stream)
+
+
 # ---------------------------------------------------------------------------
 # Type-state builder (src/inference.rs:83-196)
 # ---------------------------------------------------------------------------
@@ -475,8 +499,7 @@ class InferenceEngine:
                 raise IrodoriError(2, "Shape mismatch: out must be a contiguous [B, S, P] tensor")
             res = out
             o_p, o_mem = out.data_ptr(), MEM_DEVICE if out.is_cuda else MEM_HOST
-        st = ctypes.c_void_p(stream) if isinstance(stream, int) else (
-            ctypes.c_void_p(stream.cuda_stream) if stream is not None else None)
+        st = _stream_arg(stream, self._device, r.memory == MEM_DEVICE or o_mem == MEM_DEVICE, self)
         _check(lib().irt_engine_sample(self._h.h, ctypes.byref(r), ctypes.c_void_p(o_p), o_mem, st))
         return res
 
@@ -529,7 +552,7 @@ class DacVaeCodec:
             o_p, o_mem = out.data_ptr(), MEM_DEVICE if out.is_cuda else MEM_HOST
             if o_mem != (MEM_DEVICE if dev else MEM_HOST):
                 raise IrodoriError(22, "latent and out must live in the same memory")
-        st = ctypes.c_void_p(stream.cuda_stream) if stream is not None else None
+        st = _stream_arg(stream, self._device, bool(dev) or o_mem == MEM_DEVICE, self)
         if lengths is None:
             _check(lib().irt_codec_decode(self._h, ctypes.c_void_p(p), B, T, ctypes.c_void_p(o_p),
                                           MEM_DEVICE if dev else MEM_HOST, st))
@@ -547,16 +570,31 @@ def decode_noalloc(codec: DacVaeCodec, latent, wav, stream=None):
     """Allocation-free decode (``irt_codec_decode_noalloc``) for callers that
     cannot allocate device memory mid-decode (streaming loops that cannot
     absorb cudaMalloc/cudaFree synchronisation, hosts whose allocator owns the
-    free HBM).  ``latent`` [B, T, 32] and ``wav`` [B, 1, T * hop] are CUDA
-    tensors; B * T is limited by a fixed 16 MiB device scratch array (7 frames
-    for the full-width DACVAE).  Calls that overlap on the GPU race on that
-    array.  Returns ``wav``."""
-    B, T, C = latent.shape
-    if C != 32 or tuple(wav.shape) != (B, 1, T * codec.hop_length()):
+    free HBM).  ``latent`` [B, T, 32] and ``wav`` [B, 1, T * hop] are
+    contiguous float32 CUDA tensors on the codec's GPU; nothing is converted or
+    copied here (a conversion would allocate).  B * T is limited by a fixed
+    16 MiB device scratch array (7 frames for the full-width DACVAE).  Calls
+    that overlap on the GPU race on that array.  With ``stream=None`` the call
+    is ordered after torch's current stream.  Returns ``wav``."""
+    import torch
+    for name, t in (("latent", latent), ("wav", wav)):
+        if not isinstance(t, torch.Tensor):
+            raise IrodoriError(22, f"decode_noalloc: {name} must be a torch tensor")
+        if t.dtype != torch.float32:
+            raise IrodoriError(9, f"decode_noalloc: {name} must be float32, got {t.dtype}")
+        if not t.is_contiguous():
+            raise IrodoriError(22, f"decode_noalloc: {name} must be contiguous")
+    if latent.dim() != 3 or latent.shape[2] != 32:
+        raise IrodoriError(2, "Shape mismatch: latent must be [B, T, 32]")
+    B, T, _ = latent.shape
+    if tuple(wav.shape) != (B, 1, T * codec.hop_length()):
         raise IrodoriError(2, "Shape mismatch: latent [B, T, 32] and wav [B, 1, T * hop]")
-    lat = latent.contiguous()
-    st = ctypes.c_void_p(stream.cuda_stream) if stream is not None else None
-    _check(lib().irt_codec_decode_noalloc(codec._h, ctypes.c_void_p(lat.data_ptr()), B, T,
+    for name, t in (("latent", latent), ("wav", wav)):
+        if not t.is_cuda or t.device.index != codec._device:
+            raise IrodoriError(22, f"decode_noalloc: {name} must be a CUDA tensor on the codec's GPU "
+                                   f"(cuda:{codec._device}), got {t.device}")
+    st = _stream_arg(stream, codec._device, True, codec)
+    _check(lib().irt_codec_decode_noalloc(codec._h, ctypes.c_void_p(latent.data_ptr()), B, T,
                                           ctypes.c_void_p(wav.data_ptr()), st))
     return wav
 

@@ -333,6 +333,7 @@ Codec::Codec(int dev, const std::string& path, int precision) : device(dev), pre
     }
     tc = ok;
   }
+  codec_noalloc_prepare();
 }
 
 Codec::~Codec() {

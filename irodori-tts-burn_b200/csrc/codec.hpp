@@ -33,6 +33,7 @@ void pack_latent_rows(const float* lat, const int* frame_src, bf16* out, int F, 
 void codec_head_rows(const bf16* x, int R, int C, const float* w, const float* bias, int K, int pad,
                      const int* frame_src, int hop, float* wav, cudaStream_t s);
 int conv_tc_read_and_clear_error();
+int conv_watchdog_probe(unsigned long long limit_ns, int waits, unsigned long long* elapsed_ns);
 
 struct Codec {
   struct Conv {
@@ -78,5 +79,8 @@ struct Codec {
 // Allocation-free decode into a fixed device scratch array (codec_noalloc.cu).
 void codec_decode_noalloc(Codec& c, const float* latent, int B, int T, float* wav, cudaStream_t s);
 size_t codec_noalloc_scratch_floats();
+// Resolves the scratch array's address on the current device (best effort;
+// called by the Codec constructor with its device current).
+void codec_noalloc_prepare();
 
 }  // namespace irt

@@ -18,15 +18,22 @@
 //    upsampling so far); for the full-width DACVAE that is B * T * 96 * 1920,
 //    so B * T <= 7 latent frames (280 ms of audio) per call.  Larger requests
 //    are rejected with IRT_E_SHAPE before anything runs.
+//  - latent and wav must be device memory of the codec's own GPU (or managed
+//    memory): the kernels read and write them in place, with no staging copy.
 //  - All calls on a device share the one array and it keeps the previous
 //    call's contents; no part of it needs to start at zero because every
 //    kernel writes its whole output before that output is read.  Calls that
 //    overlap on the GPU (other host threads, other streams, other codec
 //    objects on the same device) race on the array and must be serialised by
 //    the caller.
-//  - The first call on a device resolves the array's device address with
-//    cudaGetSymbolAddress (once per device, with that device current); make
-//    that first call before any stream capture.
+//  - The array's device address is resolved with cudaGetSymbolAddress once per
+//    device, with that device current, when a codec is created on it
+//    (irt_codec_create): under lazy module loading that is the moment the
+//    16 MiB array is placed on the GPU, so a host whose allocator later takes
+//    the free HBM still finds it there.  If that early resolution failed, the
+//    first decode_noalloc call on the device retries it.
+//  - A call ends with a synchronisation of its stream, so it cannot be
+//    recorded into a CUDA graph by stream capture.
 #include <mutex>
 
 #include "codec.hpp"
@@ -60,18 +67,34 @@ float* scratch_for_current_device() {
   return g_scratch_ptr[dev];
 }
 
-bool is_device_pointer(const void* p) {
+// True for managed memory, or device memory allocated on `device`.  A device
+// pointer of another GPU is rejected: the kernels would dereference it from
+// this GPU (no staging copy on this path).
+bool is_device_pointer_on(const void* p, int device) {
   cudaPointerAttributes at{};
   if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
     cudaGetLastError();  // reset the error the failed query left behind
     return false;
   }
-  return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+  if (at.type == cudaMemoryTypeManaged) return true;
+  return at.type == cudaMemoryTypeDevice && at.device == device;
 }
 
 }  // namespace
 
 size_t codec_noalloc_scratch_floats() { return CODEC_NOALLOC_SCRATCH_FLOATS; }
+
+// Resolve the scratch address for the current device ahead of the first
+// decode_noalloc call (called when a codec is created).  A failure here is not
+// an error of codec creation: it is cleared and the first decode_noalloc call
+// retries and reports it.
+void codec_noalloc_prepare() {
+  try {
+    (void)scratch_for_current_device();
+  } catch (const Error&) {
+    cudaGetLastError();
+  }
+}
 
 // Decode `latent` [B, T, 32] (device) into `wav` [B, 1, T * hop] (device) using
 // only the static scratch array.  Returns after the result is complete.
@@ -79,8 +102,10 @@ void codec_decode_noalloc(Codec& c, const float* latent, int B, int T, float* wa
   std::lock_guard<std::mutex> lock(c.mu);
   IRT_CUDA(cudaSetDevice(c.device));
   if (B <= 0 || T <= 0) throw shape_error("decode needs batch > 0 and frames > 0");
-  if (!is_device_pointer(latent) || !is_device_pointer(wav))
-    throw Error(IRT_E_INVALID_ARG, "decode_noalloc needs device (or managed) latent and wav buffers");
+  if (!is_device_pointer_on(latent, c.device) || !is_device_pointer_on(wav, c.device))
+    throw Error(IRT_E_INVALID_ARG,
+                "decode_noalloc needs latent and wav in device memory of the codec's GPU (" +
+                    std::to_string(c.device) + ") or in managed memory");
   long maxel = (long)B * T * std::max(32, c.qout.cout);
   long t = T;
   maxel = std::max(maxel, (long)B * c.stem.cout * t);

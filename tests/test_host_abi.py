@@ -125,3 +125,34 @@ def test_config4_workload_shape(synth):
     utts = synth.throughput_utterances(64, seed=4)
     assert len(utts) == 64
     assert all(16 <= tl <= 256 and 50 <= S <= 750 and 125 <= rf <= 375 for tl, S, rf, _ in utts)
+
+
+class _FakeCodec:
+    """Stands in for a DacVaeCodec: the argument checks of decode_noalloc run
+    before any call into the library."""
+    _device = 0
+    _h = None
+
+    def hop_length(self):
+        return 1920
+
+
+def test_decode_noalloc_rejects_bad_arguments_before_the_c_call(pkg):
+    import torch
+    c = _FakeCodec()
+    lat = torch.zeros(1, 2, 32)
+    wav = torch.zeros(1, 1, 2 * 1920)
+    cases = [
+        (lat.half(), wav, "Dtype", "latent must be float32"),
+        (lat, wav.double(), "Dtype", "wav must be float32"),
+        (lat, torch.zeros(1, 1, 2 * 1920 * 2)[..., ::2], "InvalidArgument", "wav must be contiguous"),
+        (torch.zeros(1, 32, 2).transpose(1, 2), wav, "InvalidArgument", "latent must be contiguous"),
+        (torch.zeros(1, 2, 16), wav, "Shape", "latent must be"),
+        (lat, torch.zeros(1, 1, 1920), "Shape", "wav"),
+        (lat, wav, "InvalidArgument", "CUDA tensor on the codec's GPU"),  # host tensors
+        (lat.numpy(), wav, "InvalidArgument", "torch tensor"),
+    ]
+    for la, wa, kind, msg in cases:
+        with pytest.raises(pkg.IrodoriError) as ei:
+            pkg.decode_noalloc(c, la, wa)
+        assert ei.value.kind == kind and msg in str(ei.value), (kind, str(ei.value))
