@@ -385,4 +385,10 @@ void attention_tc(const AttnParams& p, cudaStream_t s) {
 
 int read_and_clear_attn_error() { return read_and_clear_flag(); }
 
+int attn_watchdog_probe(unsigned long long limit_ns, int waits, unsigned long long* elapsed_ns) {
+  const cudaError_t e = tcx::run_watchdog_probe(limit_ns, waits, elapsed_ns);
+  if (e != cudaSuccess) throw Error(IRT_E_CUDA, std::string("watchdog probe: ") + cudaGetErrorString(e));
+  return 0;
+}
+
 }  // namespace irt

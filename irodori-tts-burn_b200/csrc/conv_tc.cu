@@ -395,4 +395,10 @@ void codec_head_rows(const bf16* x, int R, int C, const float* w, const float* b
 
 int conv_tc_read_and_clear_error() { return tcx::read_and_clear_flag(); }
 
+int conv_watchdog_probe(unsigned long long limit_ns, int waits, unsigned long long* elapsed_ns) {
+  const cudaError_t e = tcx::run_watchdog_probe(limit_ns, waits, elapsed_ns);
+  if (e != cudaSuccess) throw Error(IRT_E_CUDA, std::string("watchdog probe: ") + cudaGetErrorString(e));
+  return 0;
+}
+
 }  // namespace irt

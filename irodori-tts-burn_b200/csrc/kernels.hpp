@@ -77,8 +77,14 @@ void epilogue_apply(const EpiParams& p, const float* raw, long ldr, long r_bstri
 bool gemm_tc_supported(const EpiParams& p, int K, long lda, long ldb, const void* A, const void* B);
 void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int K, const EpiParams& p,
              cudaStream_t s);
-// Device-side watchdog flag shared by the pipelined kernels (0 = ok).
+// Device-side watchdog flag of the GEMM kernels (0 = ok).
 int read_and_clear_kernel_error();
+// Watchdog probes (test hooks): run tcx::watchdog_probe_kernel in the GEMM /
+// attention translation unit with a wait limit of limit_ns and `waits` waits
+// on a barrier nothing arrives on; the elapsed device time goes to
+// *elapsed_ns and that unit's flag is left set.
+int gemm_watchdog_probe(unsigned long long limit_ns, int waits, unsigned long long* elapsed_ns);
+int attn_watchdog_probe(unsigned long long limit_ns, int waits, unsigned long long* elapsed_ns);
 
 // ---------------------------------------------------------------------------
 // Attention over [self keys | context keys] per sequence.

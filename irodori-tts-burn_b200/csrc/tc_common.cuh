@@ -14,12 +14,20 @@ namespace tcx {
 // Watchdog flag of this translation unit (each .cu that includes this header
 // has its own copy; read it with read_and_clear_flag() from the same file).
 static __device__ int g_watchdog = 0;
+// How long one mbarrier wait may spin before it gives up (ns).  4 s in
+// production; the watchdog tests shorten it with set_wait_limit_ns().
+constexpr unsigned long long DEFAULT_WAIT_LIMIT_NS = 4000000000ull;
+static __device__ unsigned long long g_wait_limit_ns = DEFAULT_WAIT_LIMIT_NS;
 
 static inline int read_and_clear_flag() {
   int v = 0, z = 0;
   cudaMemcpyFromSymbol(&v, g_watchdog, sizeof(int));
   if (v) cudaMemcpyToSymbol(g_watchdog, &z, sizeof(int));
   return v;
+}
+
+static inline cudaError_t set_wait_limit_ns(unsigned long long ns) {
+  return cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns));
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -50,20 +58,24 @@ __device__ __forceinline__ uint64_t globaltimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait: returns once the phase completes, or after ~4 s with the
-// watchdog flag set (the kernel then runs to completion with invalid data
-// instead of hanging the GPU).  Once the flag is set every later wait of this
-// translation unit's kernels gives up at once, so a stalled launch ends within
+// Bounded wait: returns once the phase completes, or after g_wait_limit_ns
+// (4 s) with the watchdog flag set (the kernel then runs to completion with
+// invalid data instead of hanging the GPU).  Once the flag is set every later
+// wait of this translation unit's kernels gives up at once (also a wait that
+// is already spinning, checked between polls), so a stalled launch ends within
 // about one timeout rather than one per wait.
 __device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return;
-  if (*reinterpret_cast<volatile int*>(&g_watchdog)) return;
+  volatile int* flag = reinterpret_cast<volatile int*>(&g_watchdog);
+  if (*flag) return;
+  const uint64_t limit = *reinterpret_cast<volatile unsigned long long*>(&g_wait_limit_ns);
   const uint64_t t0 = globaltimer();
   for (;;) {
 #pragma unroll 1
     for (int i = 0; i < 256; ++i)
       if (mbar_try_wait(bar, parity)) return;
-    if (globaltimer() - t0 > 4000000000ull) {
+    if (*flag) return;
+    if (globaltimer() - t0 > limit) {
       atomicExch(&g_watchdog, 1);
       return;
     }
@@ -113,6 +125,64 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
+
+// CTA-pair forms (cta_group::2).  The MMA and its commits are issued by the
+// pair's rank-0 CTA; a commit with .multicast::cluster arrives on the barrier
+// at the same shared-memory offset in every CTA of the mask (an arrival, not
+// a data load).
+__device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                              uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+// Address of the same shared-memory location in the pair's rank-0 CTA.
+__device__ __forceinline__ uint32_t map_rank0(uint32_t saddr) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(saddr));
+  return r;
+}
+// 2-D TMA load into this CTA's shared memory whose completion is counted on
+// an mbarrier of the pair's rank-0 CTA (no multicast).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_rank0, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_rank0), "r"(c0), "r"(c1)
+      : "memory");
+}
+// TMA reduce-add of a shared-memory box into global memory (f32 add performed
+// atomically by the memory system), bulk-group completion.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 // Generic-proxy shared-memory writes -> visible to the tensor core (async proxy).
@@ -140,6 +210,39 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Watchdog probe (test hook only, no product caller): one thread waits
+// `waits` times with mbar_wait on a barrier nothing arrives on and stores the
+// elapsed device time.  The first wait expires after the limit and sets this
+// translation unit's flag; every later one must then return at once.
+static __global__ void watchdog_probe_kernel(int waits, unsigned long long* elapsed_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    const uint64_t t0 = globaltimer();
+    for (int i = 0; i < waits; ++i) mbar_wait(smem_u32(&bar), 0);  // phase 0 never completes
+    *elapsed_ns = globaltimer() - t0;
+  }
+}
+
+// Runs the probe with a wait limit of limit_ns, restores the default limit
+// and leaves the flag set for the caller's read_and_clear_flag().
+static inline cudaError_t run_watchdog_probe(unsigned long long limit_ns, int waits,
+                                             unsigned long long* elapsed_ns_host) {
+  unsigned long long* d = nullptr;
+  cudaError_t e = cudaMalloc(&d, sizeof(*d));
+  if (e != cudaSuccess) return e;
+  e = set_wait_limit_ns(limit_ns);
+  if (e == cudaSuccess) {
+    watchdog_probe_kernel<<<1, 32>>>(waits, d);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(elapsed_ns_host, d, sizeof(*d), cudaMemcpyDeviceToHost);
+  }
+  const cudaError_t e2 = set_wait_limit_ns(DEFAULT_WAIT_LIMIT_NS);
+  cudaFree(d);
+  return e != cudaSuccess ? e : e2;
+}
 
 // hardware exp2 (MUFU ex2.approx, flush-to-zero)
 __device__ __forceinline__ float ex2(float x) {

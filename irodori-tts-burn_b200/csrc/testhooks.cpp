@@ -174,6 +174,31 @@ IRTT_API int irtt_sync_check() {
   });
 }
 
+// Bounded-wait probe: which = 0 GEMM, 1 attention, 2 conv translation unit.
+// Launches a kernel whose mbarrier waits (the kernels' own bounded wait) wait
+// on a barrier nothing arrives on, with the limit shortened to limit_ns; the
+// first wait expires and sets the unit's watchdog flag, the later ones give
+// up at once.  *elapsed_ns = device time of all waits.  The flag is left set:
+// the caller checks that it is reported (irtt_sync_check / the watchdog read)
+// and then cleared.
+IRTT_API int irtt_watchdog_probe(int which, unsigned long long limit_ns, int waits, unsigned long long* elapsed_ns) {
+  return guard([&] {
+    if (which == 0) irt::gemm_watchdog_probe(limit_ns, waits, elapsed_ns);
+    else if (which == 1) irt::attn_watchdog_probe(limit_ns, waits, elapsed_ns);
+    else if (which == 2) irt::conv_watchdog_probe(limit_ns, waits, elapsed_ns);
+    else throw irt::Error(IRT_E_INVALID_ARG, "which must be 0, 1 or 2");
+  });
+}
+
+// Reads and clears the watchdog flag of one translation unit (0 GEMM,
+// 1 attention, 2 conv); returns the flag's value or -1 on a bad index.
+IRTT_API int irtt_watchdog_read_and_clear(int which) {
+  if (which == 0) return irt::read_and_clear_kernel_error();
+  if (which == 1) return irt::read_and_clear_attn_error();
+  if (which == 2) return irt::conv_tc_read_and_clear_error();
+  return -1;
+}
+
 // adaLN modulate rows (ops.cu): h = x / sqrt(mean(x^2) + eps) * (1 + scale) +
 // shift, f32 in, bf16 or f32 out; device pointers, asynchronous (check with
 // irtt_sync_check()).
