@@ -45,3 +45,34 @@ def imbalance(costs: Sequence[float], bins: List[List[int]]) -> Tuple[float, flo
     loads = [sum(costs[i] for i in b) for b in bins]
     mean = sum(loads) / len(loads)
     return (max(loads) / mean if mean > 0 else 1.0), max(loads)
+
+
+# ---------------------------------------------------------------------------
+# Rank plumbing shared by bench.py and the multi-rank tests
+# ---------------------------------------------------------------------------
+
+def init_rank_group(backend: str, timeout_s: float, device=None):
+    """Join the job's process group (env:// rendezvous: RANK, WORLD_SIZE,
+    MASTER_ADDR, MASTER_PORT) with a short collective timeout, so that the
+    surviving ranks of a job whose rank died end their next collective with an
+    error instead of waiting for it.  Returns the ``torch.distributed``
+    module."""
+    import datetime
+
+    import torch.distributed as dist
+    kw = {"timeout": datetime.timedelta(seconds=timeout_s)}
+    if device is not None:
+        kw["device_id"] = device
+    dist.init_process_group(backend, **kw)
+    return dist
+
+
+def max_over_ranks(dist, value: float, device=None) -> float:
+    """Barrier, then the maximum of ``value`` over all ranks (the timing
+    reduction of a multi-GPU step: the job takes as long as its slowest
+    rank).  Raises if a rank has left the job."""
+    import torch
+    dist.barrier()
+    t = torch.tensor([float(value)], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())

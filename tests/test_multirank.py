@@ -61,3 +61,42 @@ def test_two_rank_sharding_and_max_timing():
     assert flat == list(range(64))
     assert set(gathered[0]).isdisjoint(gathered[1])
     assert tmax == 11.0
+
+
+def _failing_worker(rank, world, port, q):
+    """Rank 1 raises right after joining (before the timing barrier); rank 0
+    enters the bench's timing reduction and must get an error, not hang."""
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["RANK"] = str(rank)
+    os.environ["WORLD_SIZE"] = str(world)
+    load_pkg()
+    from irodori_b200 import sharding
+    d = sharding.init_rank_group("gloo", 5.0)
+    if rank == 1:
+        raise RuntimeError("injected worker failure before the timing barrier")
+    t0 = time.monotonic()
+    try:
+        sharding.max_over_ranks(d, 12.5)
+        q.put(("no error", time.monotonic() - t0))
+    except Exception as e:  # the collective fails: the dead rank never joins
+        q.put((type(e).__name__, time.monotonic() - t0))
+
+
+@pytest.mark.timeout(120)
+def test_rank_failure_before_barrier_does_not_hang():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    what, elapsed = q.get(timeout=90)
+    for p in procs:
+        p.join(timeout=60)
+    assert what != "no error"
+    assert elapsed < 30.0, elapsed
+    assert procs[1].exitcode != 0  # the injected failure
+    assert procs[0].exitcode == 0  # the survivor reported the error and left
