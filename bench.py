@@ -492,6 +492,16 @@ def reference_arm(args):
 # Engine arm
 # ---------------------------------------------------------------------------
 
+def require_finite(what, lat, lengths=None):
+    """Stop the run (non-zero exit, no JSON line) when sampled latents hold a
+    NaN or Inf, or are all zero, in any utterance's valid frames."""
+    import torch
+    for b in range(lat.shape[0]):
+        v = lat[b, :lengths[b]] if lengths is not None else lat[b]
+        if not bool(torch.isfinite(v).all()) or not bool((v != 0).any()):
+            raise SystemExit(f"bench: {what} of utterance {b} are not finite (or all zero); the run is invalid")
+
+
 def ensure_checkpoint(path: Path, cfg, rank, world):
     import torch
     import irodori_b200.synth as synth
@@ -526,6 +536,8 @@ def main():
                     help="profiling case: time every rank's config-4 bin of an N-way split on this one GPU")
     ap.add_argument("--latency-only", action="store_true",
                     help="only the config-3 single-utterance latency (used for profiling runs)")
+    ap.add_argument("--timeline", action="store_true",
+                    help="profiling case: kernel timeline (CUPTI activity trace) of one config-4 sample()")
     ap.add_argument("--gemm-case", type=int, default=0,
                     help="only the four DiT GEMMs of one layer at M rows, --steps times (profiling case)")
     args = ap.parse_args()
@@ -533,6 +545,8 @@ def main():
         return reference_arm(args)
     if args.latency_only:
         return latency_only(args)
+    if args.timeline:
+        return timeline_case(args)
     if args.shard:
         return shard_case(args)
     if args.row_case:
@@ -565,16 +579,14 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        # keep stdout to the one JSON line (NCCL prints its version at INFO level)
-        os.environ.setdefault("NCCL_DEBUG", "WARN")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
-
     pkg = load_pkg()
     from irodori_b200 import sharding
+    if world > 1:
+        # keep stdout to the one JSON line (NCCL prints its version at INFO level)
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        # a rank that dies makes the others' next collective fail within this
+        # timeout (checkpoint generation on rank 0 happens before the first one)
+        dist = sharding.init_rank_group("nccl", 300, device=torch.device("cuda", local))
     cfg = model_cfg()
     ckpt = Path(args.ckpt) if args.ckpt else Path(tempfile.gettempdir()) / "irodori_bench" / "dit_default_l32_s4.safetensors"
     ensure_checkpoint(ckpt, cfg, rank, world)
@@ -611,17 +623,17 @@ def main():
         e1.record(stream)
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
-        t = torch.tensor([ms], device="cuda")
         if dist is not None:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            dist.barrier()
-        return float(t.item()), launches
+            ms = sharding.max_over_ranks(dist, ms, device="cuda")
+        return ms, launches
 
     for _ in range(args.warmup):
         eng.sample(req(dev_in), out=out_dev, stream=stream)
     torch.cuda.synchronize()
+    require_finite("warm-up latents", out_dev, batch["sequence_lengths"])
     with ClockSampler(local) as clk:
         ms, launches = timed(dev_in, out_dev, args.steps)
+    require_finite("timed latents", out_dev, batch["sequence_lengths"])
     clocks = clk.summary()
     ms_step = ms / args.steps
     value = audio_total * args.steps / (ms / 1000.0)
@@ -630,6 +642,7 @@ def main():
     import numpy as np
     out_host = np.empty((B, Sm, P), dtype=np.float32)
     e2e_ms, _ = timed(host_in, out_host, args.steps)
+    require_finite("e2e latents", torch.from_numpy(out_host), batch["sequence_lengths"])
     h2d = sum(v.nbytes for v in host_in.values()) + 4 * B
     d2h = out_host.nbytes
     e2e_value = audio_total * args.steps / (e2e_ms / 1000.0)
@@ -750,13 +763,18 @@ def config5(pkg, eng, cfg, stream, rank, world, dist, steps, warmup):
             step(decode_only)
         e1.record(stream)
         torch.cuda.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1) / k], device="cuda")
+        ms = e0.elapsed_time(e1) / k
         if dist is not None:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+            from irodori_b200 import sharding
+            ms = sharding.max_over_ranks(dist, ms, device="cuda")
+        return ms
 
     for _ in range(warmup):
         step(False)
+    torch.cuda.synchronize()
+    require_finite("config-5 latents", lat, lens)
+    if not bool(torch.isfinite(wav).all()):
+        raise SystemExit("bench: config-5 waveform is not finite; the run is invalid")
     ms_t2w = timed(False, steps)
     ms_dec = timed(True, steps)
     audio_job = sum(u[3] for u in utts)
@@ -855,6 +873,75 @@ def shard_case(args):
     return 0
 
 
+def timeline_case(args):
+    """Kernel timeline of one config-4 sample() on rank 0's bin at N=1: the
+    engine built as in the bench, `--warmup` untraced samples, then one
+    sample under CUDA activity tracing (torch.profiler, CUDA activities only:
+    CUPTI kernel start/end timestamps, no replay or serialisation).  Prints
+    one JSON line: span, GPU-busy time (union of kernel and copy intervals),
+    idle time, and per kernel name its launches, total and average duration
+    and share of the summed durations."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    pkg = load_pkg()
+    from irodori_b200 import sharding
+    cfg = model_cfg()
+    ckpt = Path(args.ckpt) if args.ckpt else Path(tempfile.gettempdir()) / "irodori_bench" / "dit_default_l32_s4.safetensors"
+    ensure_checkpoint(ckpt, cfg, 0, 1)
+    params = pkg.SamplerParams(num_steps=40, method="euler",
+                               guidance=pkg.GuidanceConfig(mode="joint", scale_text=3.0, scale_speaker=3.0))
+    eng = pkg.InferenceBuilder(0).load_weights(str(ckpt), precision="bf16").with_sampling(params).build()
+    utts = workload()
+    costs = [sharding.utterance_cost(S, tl, rf) for tl, S, rf, _ in utts]
+    mine = sharding.shard_for_rank(costs, 0, 1)
+    batch = build_batch(utts, mine, cfg["latent_dim"], cfg["text_vocab_size"])
+    keys = ("text_ids", "text_mask", "ref_latent", "ref_mask", "initial_noise")
+    dev_in = {k: batch[k].cuda() for k in keys}
+    out = torch.empty(len(mine), batch["sequence_length"], cfg["latent_dim"], device="cuda")
+    stream = torch.cuda.Stream()
+    rq = pkg.SamplingRequest(sequence_length=batch["sequence_length"], sequence_lengths=batch["sequence_lengths"],
+                             **dev_in)
+    for _ in range(max(1, args.warmup)):
+        eng.sample(rq, out=out, stream=stream)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        eng.sample(rq, out=out, stream=stream)
+        torch.cuda.synchronize()
+    require_finite("timeline latents", out, batch["sequence_lengths"])
+    with tempfile.TemporaryDirectory() as d:
+        fn = os.path.join(d, "trace.json")
+        prof.export_chrome_trace(fn)
+        ev = json.load(open(fn))["traceEvents"]
+    kern = [e for e in ev if e.get("cat") == "kernel" and "dur" in e]
+    busy_ev = [e for e in ev if e.get("cat") in ("kernel", "gpu_memcpy", "gpu_memset") and "dur" in e]
+    iv = sorted((float(e["ts"]), float(e["ts"]) + float(e["dur"])) for e in busy_ev)
+    busy, cur_s, cur_e = 0.0, None, None
+    for a, b in iv:
+        if cur_e is None or a > cur_e:
+            if cur_e is not None:
+                busy += cur_e - cur_s
+            cur_s, cur_e = a, b
+        else:
+            cur_e = max(cur_e, b)
+    if cur_e is not None:
+        busy += cur_e - cur_s
+    span = (iv[-1][1] - iv[0][0]) if iv else 0.0
+    per = {}
+    for e in kern:
+        n = e["name"].split("(")[0]
+        c, t = per.get(n, (0, 0.0))
+        per[n] = (c + 1, t + float(e["dur"]))
+    total = sum(t for _, t in per.values())
+    rows = sorted(per.items(), key=lambda kv: -kv[1][1])
+    print(json.dumps({"timeline": "config4 rank-0 bin at N=1, one sample()", "span_ms": round(span / 1e3, 1),
+                      "busy_ms": round(busy / 1e3, 1), "idle_ms": round((span - busy) / 1e3, 2),
+                      "kernel_sum_ms": round(total / 1e3, 1),
+                      "kernels": [{"name": n, "launches": c, "total_ms": round(t / 1e3, 2),
+                                   "avg_us": round(t / c, 1), "share": round(t / total, 4)} for n, (c, t) in rows]}),
+          flush=True)
+    return 0
+
+
 def latency_only(args):
     """Config-3 latency alone: one checkpoint load, `--warmup` untimed and
     `--steps` timed sample() calls for the default CFG window."""
@@ -913,6 +1000,7 @@ def latency_config3(pkg, eng, cfg, stream, reps=3):
             e1.record(stream)
             torch.cuda.synchronize()
             ts.append(e0.elapsed_time(e1))
+        require_finite(f"config-3 latents ({name})", out)
         res[name] = round(min(ts), 2)
     eng.with_sampling(keep)
     res["row_forwards_min_t_0.5"] = 60

@@ -455,6 +455,9 @@ void Engine::forward_step(int M, const SeqDesc* d_seqs, int nseq, int max_len, i
       (uintptr_t)ws.rope_cos.p, (uintptr_t)ws.rope_sin.p, (uintptr_t)ada_cur.p};
   auto it = graphs.find(key);
   if (it == graphs.end()) {
+    // keys seen once and never again (a server sees many ragged shapes) must
+    // not accumulate: the table of first uses is bounded like the graphs
+    if (graph_seen.size() > 256) graph_seen.clear();
     if (graph_seen[key]++ == 0) {  // first use: eager (allocations happen here)
       dit_forward(M, d_seqs, nseq, max_len, ada_cur.as<float>(), nrows_ctx, s);
       return;
@@ -477,7 +480,9 @@ void Engine::forward_step(int M, const SeqDesc* d_seqs, int nseq, int max_len, i
     if (graphs.size() > 64) {  // bound the cache
       for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
       graphs.clear();
+      graph_kernels.clear();
     }
+    graph_seen.erase(key);
     it = graphs.emplace(key, ge).first;
     // kernels recorded in the graph (captured launches are not executed)
     graph_kernels[key] = launch_counter().load() - before;
