@@ -441,6 +441,88 @@ def cpu_block_sample(target_s=12.0):
     return per, flops, torch.get_num_threads(), sample
 
 
+def cpu_model():
+    """The host CPU's model name and the number of cores this process may use."""
+    name = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    name = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return name, len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+
+def config1_case(pkg):
+    """BASELINE config 1 run end to end, no extrapolation: the reference's
+    default ModelConfig (latent 128) with random-init weights (seed 0,
+    N(0, 0.02), zero-init adaLN up-projections), batch 1, text 64 ids, speaker
+    reference 150 frames ~N(0, 1), 250 target frames (10 s) with initial noise
+    seed 1, 4 Euler steps with independent CFG (text 3, speaker 3).  The CPU
+    oracle (f32, all host threads) runs the whole sampler -- both condition
+    encoders, the context KV caches, 8 DiT row-forwards -- once; the engine
+    runs the same request on the GPU (bf16 and f32 modes, CUDA events, best
+    of 3 after a warm-up).  Returns the JSON object of the bench line."""
+    import torch
+    import numpy as np
+    from oracle import irodori_oracle as O
+    import irodori_b200.synth as synth
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    path = Path(tempfile.gettempdir()) / "irodori_bench" / "dit_default_config1_s0.safetensors"
+    if not path.exists():
+        path.parent.mkdir(parents=True, exist_ok=True)
+        synth.make_dit_checkpoint(str(path), {}, seed=0, init="baseline", dtype=torch.bfloat16, device="cuda")
+        torch.cuda.synchronize()
+    r = synth.make_request({}, 1, 64, 150, 250, seed=1)
+    W = O.Weights.load(str(path))
+    req = O.SamplingRequest(text_ids=r["text_ids"], text_mask=r["text_mask"], sequence_length=250,
+                            ref_latent=r["ref_latent"], ref_mask=r["ref_mask"], initial_noise=r["initial_noise"])
+    op = O.SamplerParams(num_steps=4, guidance=O.GuidanceConfig(mode="independent", scale_text=3.0,
+                                                                 scale_speaker=3.0))
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        ref = O.sample_euler_rf_cfg(W, req, op)
+        cpu_s = time.perf_counter() - t0
+    del W
+    audio = 250 / FRAME_RATE
+    gpu = {}
+    d = {k: v.cuda() for k, v in r.items() if torch.is_tensor(v)}
+    out = torch.empty(1, 250, 128, device="cuda")
+    for prec in ("bf16", "f32"):
+        eng = (pkg.InferenceBuilder(0).load_weights(str(path), precision=prec)
+               .with_sampling(pkg.SamplerParams(num_steps=4, guidance=pkg.GuidanceConfig(
+                   mode="independent", scale_text=3.0, scale_speaker=3.0))).build())
+        rq = pkg.SamplingRequest(sequence_length=250, **d)
+        st = torch.cuda.current_stream()
+        eng.sample(rq, out=out, stream=st)
+        ts = []
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            eng.sample(rq, out=out, stream=st)
+            e1.record(st)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        require_finite(f"config-1 latents ({prec})", out)
+        o = out.cpu().numpy().astype(np.float64)
+        rv = ref.numpy().astype(np.float64)
+        gpu[prec] = {"ms": round(min(ts), 2), "audio_s_per_s": round(audio / (min(ts) / 1000.0), 1),
+                     "rel_l2_vs_cpu_oracle": float("%.3e" % (np.linalg.norm(o - rv) / np.linalg.norm(rv)))}
+        del eng
+    name, cores = cpu_model()
+    return {"workload": "config1: default ModelConfig (latent 128), random init seed 0, batch 1, text 64, speaker "
+                        "150 frames, 250 target frames (10 s), 4 Euler steps, independent CFG 3/3; whole sampler "
+                        "(encoders, KV caches, 8 row-forwards)",
+            "cpu_oracle": {"seconds": round(cpu_s, 2), "audio_s_per_s": round(audio / cpu_s, 4), "dtype": "f32",
+                           "threads": threads, "cpu_model": name, "cores_available": cores,
+                           "kind": "port (CPU restatement of the reference sampler; the Rust crate has no "
+                                   "toolchain here)"},
+            "gpu_engine": gpu}
+
+
 def job_flops(utts, min_t=0.5, steps=40):
     """Algorithmic FLOPs of the whole config-4 job (joint CFG: cond row with all
     valid keys, uncond row with the latent keys only, in the CFG window)."""
@@ -478,11 +560,15 @@ def reference_arm(args):
         if i >= args.warmup:
             vals.append(audio / (per * total / fl))
     v = statistics.median(vals)
+    # one step = the whole config-4 job on the host cores (extrapolated from
+    # the timed block sample), so ms_per_step * value = audio seconds * 1000
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(audio / v * 1000.0, 1),
+            "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": config4_dict(audio, args.gpus),
-            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "cpu_model": cpu_model()[0],
+                             "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -687,10 +773,13 @@ def main():
         lat = latency_config3(pkg, eng, cfg, stream)
 
     cpu = None
+    c1 = None
     if world == 1 and not args.skip_cpu:
         per, fl, threads, sample = cpu_block_sample()
+        name, _ = cpu_model()
         cpu = {"value": audio_total / (per * total_flops / fl), "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": sample}
+               "cpu_model": name, "sample": sample}
+        c1 = config1_case(pkg)
 
     line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 2), "higher_is_better": True, "scaling": "strong",
@@ -699,7 +788,7 @@ def main():
             "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
-            "latency_config3": lat, "config5": c5, **extra}
+            "latency_config3": lat, "config5": c5, "config1": c1, **extra}
     print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
@@ -928,7 +1017,7 @@ def timeline_case(args):
     span = (iv[-1][1] - iv[0][0]) if iv else 0.0
     per = {}
     for e in kern:
-        n = e["name"].split("(")[0]
+        n = e["name"].replace("(anonymous namespace)", "").split("(")[0]
         c, t = per.get(n, (0, 0.0))
         per[n] = (c + 1, t + float(e["dur"]))
     total = sum(t for _, t in per.values())

@@ -240,9 +240,12 @@ void Engine::load(const std::string& path, const std::string& adapter_dir) {
   upload_rows(stg, lin("cond_module.linear2.weight", 3 * D, D), cm2.p, 0, D, 0, 0, 0);
 
   Pk = (bf && P % 64) ? (P + 63) / 64 * 64 : P;
-  in_w.alloc((size_t)D * Pk * es);
-  IRT_CUDA(cudaMemset(in_w.p, 0, (size_t)D * Pk * es));  // zero K padding
-  upload_rows(stg, lin("in_proj.weight", D, P), in_w.p, bf, Pk, 0, 0, 0);
+  Kin = bf ? 2 * Pk : Pk;
+  in_w.alloc((size_t)D * Kin * es);
+  IRT_CUDA(cudaMemset(in_w.p, 0, (size_t)D * Kin * es));  // zero K padding
+  upload_rows(stg, lin("in_proj.weight", D, P), in_w.p, bf, Kin, 0, 0, 0);
+  if (bf)  // the same weight again under the lo half of the operand
+    upload_rows(stg, lin("in_proj.weight", D, P), static_cast<uint8_t*>(in_w.p) + (size_t)Pk * es, bf, Kin, 0, 0, 0);
   f32vec(in_b, "in_proj.bias", D);
 
   const char* kinds[3] = {"shift", "scale", "gate"};
@@ -311,9 +314,13 @@ void Engine::load(const std::string& path, const std::string& adapter_dir) {
   out_w.alloc((size_t)P * D * es);
   upload_rows(stg, lin("out_proj.weight", P, D), out_w.p, bf, D, 0, 0, 0);
   if (bf && P <= 128) {
-    out_w_pad.alloc((size_t)128 * D * es);
-    IRT_CUDA(cudaMemset(out_w_pad.p, 0, (size_t)128 * D * es));
-    IRT_CUDA(cudaMemcpy(out_w_pad.p, out_w.p, (size_t)P * D * es, cudaMemcpyDeviceToDevice));
+    out_split = rms_norm_split_supported(D);
+    const size_t kw = out_split ? 2 * (size_t)D : (size_t)D;  // [W | W] along K when split
+    out_w_pad.alloc(128 * kw * es);
+    IRT_CUDA(cudaMemset(out_w_pad.p, 0, 128 * kw * es));
+    for (int part = 0; part < (out_split ? 2 : 1); ++part)
+      IRT_CUDA(cudaMemcpy2D(static_cast<uint8_t*>(out_w_pad.p) + (size_t)part * D * es, kw * es, out_w.p,
+                            (size_t)D * es, (size_t)D * es, P, cudaMemcpyDeviceToDevice));
   }
   f32vec(out_b, "out_proj.bias", P);
   IRT_CUDA(cudaDeviceSynchronize());
@@ -502,7 +509,7 @@ void Engine::dit_forward(int M, const SeqDesc* d_seqs, int nseq, int max_len, co
     p.out = x;
     p.ldo = D;
     p.bias = in_b.as<float>();
-    gemm(ws.xin.p, Pk, in_w, M, D, Pk, p, s);
+    gemm(ws.xin.p, Kin, in_w, M, D, Kin, p, s);
   }
   float* dump = dump_layers;
   if (dump) {
@@ -568,8 +575,13 @@ void Engine::dit_forward(int M, const SeqDesc* d_seqs, int nseq, int max_len, co
   op.bias = out_b.as<float>();
   if (out_w_pad.p && M >= 128 && (D % 64) == 0) {
     // out_norm (RmsNorm, bf16 rows) then out_proj on the tensor cores
-    rms_norm(x, out_norm.as<float>(), ws.h.p, 1, M, D, eps, s);
-    gemm_tc(ws.h.as<bf16>(), D, out_w_pad.as<bf16>(), D, M, 128, D, op, s);
+    if (out_split) {
+      rms_norm_split(x, out_norm.as<float>(), ws.hm.as<bf16>(), M, D, eps, s);
+      gemm_tc(ws.hm.as<bf16>(), 2 * D, out_w_pad.as<bf16>(), 2 * D, M, 128, 2 * D, op, s);
+    } else {
+      rms_norm(x, out_norm.as<float>(), ws.h.p, 1, M, D, eps, s);
+      gemm_tc(ws.h.as<bf16>(), D, out_w_pad.as<bf16>(), D, M, 128, D, op, s);
+    }
   } else {
     rmsnorm_proj(x, out_norm.as<float>(), out_w.p, bf, out_b.as<float>(), ws.vout.as<float>(), M, D, P, eps, s);
   }
@@ -931,9 +943,9 @@ void Engine::sample(const irt_request& rq, float* out, int out_memory, cudaStrea
   ws.v.ensure((size_t)Mmax * D * esz());
   ws.g.ensure((size_t)Mmax * D * esz());
   ws.attn.ensure((size_t)Mmax * D * esz());
-  ws.hm.ensure((size_t)Mmax * F * esz());
-  ws.xin.ensure((size_t)Mmax * Pk * esz());
-  if (Pk != P) IRT_CUDA(cudaMemsetAsync(ws.xin.p, 0, (size_t)Mmax * Pk * esz(), s));  // zero K padding
+  ws.hm.ensure((size_t)Mmax * std::max(F, out_split ? 2 * D : 0) * esz());  // also the split out_norm rows
+  ws.xin.ensure((size_t)Mmax * Kin * esz());
+  if (Kin != P) IRT_CUDA(cudaMemsetAsync(ws.xin.p, 0, (size_t)Mmax * Kin * esz(), s));  // zero K padding
   ws.vout.ensure((size_t)Mmax * P * 4);
   ws.tokpos.ensure((size_t)Mmax * 4);
   {
@@ -1036,8 +1048,11 @@ void Engine::sample(const irt_request& rq, float* out, int out_memory, cudaStrea
     int G = (int)groups.size();
     int toff = table_off.at(groups);
     // replicate x into each group's rows
-    for (int g = 0; g < G; ++g)
-      gather_rows(xin_f32, nullptr, ws.xin.as<uint8_t>() + (size_t)g * ntok * Pk * esz(), bf, ntok, P, s, Pk);
+    for (int g = 0; g < G; ++g) {
+      uint8_t* dst = ws.xin.as<uint8_t>() + (size_t)g * ntok * Kin * esz();
+      if (bf) gather_split_rows(xin_f32, reinterpret_cast<bf16*>(dst), ntok, P, Pk, s);
+      else gather_rows(xin_f32, nullptr, dst, 0, ntok, P, s, Pk);
+    }
     forward_step(G * ntok, ws.seqs.as<SeqDesc>() + toff, G * B, Smax, t_index, nctx, s);
     last_row_forwards += (long long)G * B;
     if (G == 1) {

@@ -49,6 +49,14 @@ struct Engine {
   // in_proj reduction width: P, or (bf16 mode) P zero-padded to a multiple of
   // 64 so the projection runs on the tcgen05 GEMM with its bias epilogue
   int Pk = 0;
+  // in_proj GEMM reduction width: Pk in f32 mode; 2 Pk in bf16 mode, where the
+  // f32 latent x_t enters as bf16 hi | lo halves over the weight stored twice
+  // ([W | W] along K), so the projection is not limited by one bf16 rounding
+  // of x_t (the sampler state)
+  int Kin = 0;
+  // bf16 mode: out_norm rows enter out_proj as bf16 hi | lo halves over
+  // out_w_pad = [W | W] (K = 2 D), for the same reason on the velocity
+  bool out_split = false;
   int aux_kind = 0;  // 0 none, 1 speaker, 2 caption
   int aux_dim = 0;
 

@@ -128,6 +128,12 @@ void adaln_modulate(const float* x, const float* shift, const float* scale, void
                     float eps, cudaStream_t s);
 // y = x / sqrt(mean(x^2)+eps) * w   (RmsNorm; w may be null)
 void rms_norm(const float* x, const float* w, void* y, int out_bf16, int M, int D, float eps, cudaStream_t s);
+// RMSNorm rows written as bf16 hi | lo halves ([M, 2D]) for a GEMM over the
+// weight repeated along K; D a multiple of 4, at most 2048.
+bool rms_norm_split_supported(int D);
+void rms_norm_split(const float* x, const float* w, bf16* y, int M, int D, float eps, cudaStream_t s);
+// f32 rows [M, P] -> bf16 hi | lo rows [M, 2 Pk] (hi at column d, lo at Pk + d).
+void gather_split_rows(const float* in, bf16* out, int M, int P, int Pk, cudaStream_t s);
 // out = RmsNorm(x; nw) . W^T + bias for a narrow output (W [P, D], bf16 or f32)
 void rmsnorm_proj(const float* x, const float* nw, const void* W, int w_bf16, const float* bias, float* out, int M,
                   int D, int P, float eps, cudaStream_t s);

@@ -83,7 +83,11 @@ __global__ void __launch_bounds__(NT) rownorm_kernel(const float* __restrict__ x
 
 // Register-resident variant: each thread keeps up to VPT float4 of the row,
 // so the row is read from memory once.  Same arithmetic as rownorm_kernel.
-template <int NT, int VPT, bool OBF>
+// SPLIT (bf16 output only): the row is written as two bf16 halves, hi =
+// bf16(v) in columns [0, D) and lo = bf16(v - hi) in [D, 2D) of a 2D-wide row,
+// for a GEMM whose weight is repeated along K ([W | W]): hi*W + lo*W carries
+// the f32 value to ~2^-16 instead of one bf16 rounding.
+template <int NT, int VPT, bool OBF, bool SPLIT = false>
 __global__ void __launch_bounds__(NT) rownorm_reg_kernel(const float* __restrict__ x, const float* __restrict__ a,
                                                          const float* __restrict__ b, void* __restrict__ y, int D,
                                                          float eps, int mode) {
@@ -126,7 +130,19 @@ __global__ void __launch_bounds__(NT) rownorm_reg_kernel(const float* __restrict
       uint2 u;
       u.x = *reinterpret_cast<uint32_t*>(&p0);
       u.y = *reinterpret_cast<uint32_t*>(&p1);
-      reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(y) + row * D)[c] = u;
+      if (SPLIT) {
+        const float2 h0 = __bfloat1622float2(p0), h1 = __bfloat1622float2(p1);
+        __nv_bfloat162 l0 = __floats2bfloat162_rn(o[0] - h0.x, o[1] - h0.y);
+        __nv_bfloat162 l1 = __floats2bfloat162_rn(o[2] - h1.x, o[3] - h1.y);
+        uint2 ul;
+        ul.x = *reinterpret_cast<uint32_t*>(&l0);
+        ul.y = *reinterpret_cast<uint32_t*>(&l1);
+        bf16* yr = reinterpret_cast<bf16*>(y) + row * 2 * D;
+        reinterpret_cast<uint2*>(yr)[c] = u;
+        reinterpret_cast<uint2*>(yr + D)[c] = ul;
+      } else {
+        reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(y) + row * D)[c] = u;
+      }
     } else {
       reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + row * D)[c] = make_float4(o[0], o[1], o[2], o[3]);
     }
@@ -253,6 +269,19 @@ __global__ void gather_kernel(const float* in, const int* src, void* out, int ou
   else reinterpret_cast<float*>(out)[o] = v;
 }
 
+// f32 rows [M, P] -> bf16 [M, 2 Pk]: hi = bf16(v) at column d, lo = bf16(v - hi)
+// at column Pk + d (padding columns are left untouched).
+__global__ void gather_split_kernel(const float* in, bf16* out, int M, int P, int Pk) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)M * P) return;
+  const int m = (int)(i / P), d = (int)(i % P);
+  const float v = in[i];
+  const bf16 hi = __float2bfloat16_rn(v);
+  bf16* o = out + (long)m * 2 * Pk;
+  o[d] = hi;
+  o[Pk + d] = __float2bfloat16_rn(v - __bfloat162float(hi));
+}
+
 __global__ void mask_rows_kernel(float* x, const uint8_t* mask, int M, int D) {
   long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long)M * D) return;
@@ -372,6 +401,14 @@ void adaln_modulate(const float* x, const float* shift, const float* scale, void
 void rms_norm(const float* x, const float* w, void* y, int out_bf16, int M, int D, float eps, cudaStream_t s) {
   rownorm(x, w, nullptr, y, out_bf16, M, D, eps, 0, s);
 }
+bool rms_norm_split_supported(int D) { return D % 4 == 0 && D / 4 <= 128 * 4; }
+void rms_norm_split(const float* x, const float* w, bf16* y, int M, int D, float eps, cudaStream_t s) {
+  if (M <= 0) return;
+  if (!rms_norm_split_supported(D)) throw unsupported("rms_norm_split: D must be a multiple of 4 and <= 2048");
+  launch_pdl(rownorm_reg_kernel<128, 4, true, true>, dim3(M), dim3(128), 0, s, x, w, (const float*)nullptr,
+             (void*)y, D, eps, 0);
+  IRT_CHECK_LAUNCH();
+}
 void rmsnorm_proj(const float* x, const float* nw, const void* W, int w_bf16, const float* bias, float* out, int M,
                   int D, int P, float eps, cudaStream_t s) {
   if (M <= 0) return;
@@ -400,6 +437,11 @@ void gather_rows(const float* in, const int* src_row, void* out, int out_bf16, i
                  int ld_out) {
   if ((long)M * D == 0) return;
   gather_kernel<<<nblk((long)M * D), 256, 0, s>>>(in, src_row, out, out_bf16, M, D, ld_out > 0 ? ld_out : D);
+  IRT_CHECK_LAUNCH();
+}
+void gather_split_rows(const float* in, bf16* out, int M, int P, int Pk, cudaStream_t s) {
+  if ((long)M * P == 0) return;
+  gather_split_kernel<<<nblk((long)M * P), 256, 0, s>>>(in, out, M, P, Pk);
   IRT_CHECK_LAUNCH();
 }
 void mask_rows(float* x, const uint8_t* mask, int M, int D, cudaStream_t s) {

@@ -48,3 +48,7 @@ def test_reference_arm_line():
     assert d["config"] == b.config4_dict(sum(u[3] for u in utts), 1)
     assert d["value"] > 0 and d["cpu_baseline"]["value"] == d["value"] and d["cpu_baseline"]["kind"] == "port"
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    # a finite step time consistent with the value (one step = the whole job's audio)
+    audio = sum(u[3] for u in utts)
+    assert d["ms_per_step"] > 0 and d["ms_per_step"] == pytest.approx(audio / d["value"] * 1000.0, rel=1e-3)
+    assert d["cpu_baseline"].get("cpu_model") is not None

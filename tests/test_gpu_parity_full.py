@@ -306,3 +306,63 @@ def test_e2e_compare_scenario_f32(pkg, oracle, synth, default_ckpt, default_w, m
     err = rel_l2(out, ref)
     print(f"e2e_compare {method} x{steps} f32: rel-L2 {err:.3e}")
     assert err < F32_TOL, err
+
+
+# ---------------------------------------------------------------------------
+# decoded waveform: bf16 sampler + bf16 codec against f32 sampler + f32 codec
+# ---------------------------------------------------------------------------
+
+def test_decoded_waveform_snr_40_steps(pkg, synth, ckpt_dir):
+    """The bench's model and sampler (default dims with the codec's 32 latent
+    channels, the bench's own random init; 40 Euler steps, joint CFG 3.0) on
+    two utterances of 100 and 175 frames sampled as one ragged batch, decoded
+    to 48 kHz by the DACVAE decoder (reference-default random init).  The f32
+    engine tracks the oracle within ~1e-5 at these dims (tests above), so the
+    f32 sampler + f32 codec stands in for the reference's output here.
+    Reported: final-latent rel-L2 of the bf16 sampler and the SNR of the bf16
+    sampler + bf16 codec waveform."""
+    p = ckpt_dir / "default_l32_bf16.safetensors"
+    synth.make_dit_checkpoint(str(p), {"latent_dim": 32}, seed=4, init="baseline", dtype=torch.bfloat16,
+                              device="cuda")
+    torch.cuda.synchronize()
+    cp = ckpt_dir / "codec_ref_init.safetensors"
+    synth.make_codec_checkpoint(str(cp), seed=5, width_div=1, init="reference")
+    cfg = dict(synth.DEFAULT_CONFIG, latent_dim=32)
+    lens = [100, 175]
+    reqs = [synth.make_request(cfg, 1, t, rf, S, seed=60 + i) for i, (t, rf, S) in enumerate([(60, 150, 100),
+                                                                                            (120, 250, 175)])]
+    Sm = max(lens)
+    ids = torch.zeros(2, 120, dtype=torch.int32)
+    tm = torch.zeros(2, 120, dtype=torch.bool)
+    ref = torch.zeros(2, 250, 32)
+    rm = torch.zeros(2, 250, dtype=torch.bool)
+    noise = torch.zeros(2, Sm, 32)
+    for b, r in enumerate(reqs):
+        T, R, S = r["text_ids"].shape[1], r["ref_latent"].shape[1], lens[b]
+        ids[b, :T], tm[b, :T] = r["text_ids"][0], True
+        ref[b, :R], rm[b, :R] = r["ref_latent"][0], True
+        noise[b, :S] = r["initial_noise"][0]
+    rq = pkg.SamplingRequest(text_ids=ids, text_mask=tm, sequence_length=Sm, ref_latent=ref, ref_mask=rm,
+                             initial_noise=noise, sequence_lengths=lens)
+    params = eparams(pkg, 40, mode="joint")
+    lat = {}
+    for prec in ("f32", "bf16"):
+        eng = engine(pkg, p, prec, params)
+        lat[prec] = eng.sample(rq)
+        del eng
+    wav = {}
+    for prec in ("f32", "bf16"):
+        codec = pkg.load_codec(str(cp), device=0, precision=prec)
+        wav[prec] = codec.decode(lat[prec], lengths=lens)
+        del codec
+    hop = 1920
+    errs, snrs = [], []
+    for b, S in enumerate(lens):
+        errs.append(rel_l2(lat["bf16"][b, :S], lat["f32"][b, :S]))
+        a, w = wav["f32"][b, 0, :S * hop].astype(np.float64), wav["bf16"][b, 0, :S * hop].astype(np.float64)
+        assert np.isfinite(w).all()
+        snrs.append(10 * np.log10(np.sum(a * a) / max(np.sum((w - a) ** 2), 1e-30)))
+    print("40-step bf16 vs f32 sampler: latent rel-L2 " + " ".join(f"{e:.2e}" for e in errs) +
+          "; decoded waveform SNR " + " ".join(f"{s:.1f} dB" for s in snrs))
+    assert max(errs) < BF16_TOL, errs
+    assert min(snrs) > 20.0, snrs
