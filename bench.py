@@ -335,8 +335,9 @@ def attn_case(steps, which="c3"):
     "c3": the config-3 CFG step (cond row: 750 queries over 750 self + 576
     context keys; uncond row: 750 over 750).  "c4": the config-4 CFG step
     (64 utterances; cond rows over self + text + speaker keys, uncond rows over
-    self keys), packed (group, utterance, frame) like the engine.  "c4p": the
-    config-4 plain step (cond rows only).  Returns (ms per launch, TFLOP/s)."""
+    self keys), packed (group, utterance, frame) like the engine.  "c4p" /
+    "c3p": the config-4 / config-3 plain step (cond rows only).  Returns (ms
+    per launch, TFLOP/s)."""
     import torch
     L = ctypes.CDLL(str(PKG_DIR / "libirodori_b200_testhooks.so"))
     L.irtt_attention.argtypes = ([ctypes.c_void_p] * 8 + [ctypes.c_int] * 3 + [ctypes.c_void_p] + [ctypes.c_int] * 4)
@@ -351,7 +352,7 @@ def attn_case(steps, which="c3"):
         ctxs = [u[0] + u[2] + 1 for u in utts]
     else:
         lens, ctxs = [750], [576]
-    uncond = which != "c4p"
+    uncond = which not in ("c4p", "c3p")
     seqs, tok, co = [], 0, 0
     for S, c in zip(lens, ctxs):  # cond rows
         seqs.append((tok, S, co, c))
@@ -612,7 +613,7 @@ def main():
     ap.add_argument("--codec-only", action="store_true",
                     help="time the config-5 DACVAE decode alone (16 utterances, seeded latents)")
     ap.add_argument("--codec-precision", default="bf16", choices=["bf16", "f32"])
-    ap.add_argument("--attn-case", nargs="?", const="c3", default=None, choices=["c3", "c4", "c4p"],
+    ap.add_argument("--attn-case", nargs="?", const="c3", default=None, choices=["c3", "c3p", "c4", "c4p"],
                     help="only the joint attention of one layer: config-3 CFG step (c3), config-4 CFG step (c4) "
                          "or config-4 plain step (c4p), --steps launches (profiling case)")
     ap.add_argument("--ckpt", default=None)

@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -38,6 +39,8 @@ int gemm_watchdog_probe(unsigned long long limit_ns, int waits, unsigned long lo
 namespace tc {
 
 constexpr int BM = 128, BK = 64, EPI_WARPS = 8, THREADS = 64 + 32 * EPI_WARPS;
+// Smallest k-block span of a group in a tail split (splits == -2).
+constexpr int TAIL_MIN_SPAN = 8;
 constexpr uint32_t A_BYTES = BM * BK * 2;
 
 // CG = CTAs per MMA: 1, or 2 for a CTA pair (cluster of 2) that computes a
@@ -100,21 +103,28 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
 // Work decomposition shared by the producer, MMA and epilogue roles.
 //  splits >= 1: units (tile, K-split) dealt round-robin to the work groups
 //    (a group = one CTA, or one CTA pair).
-//  splits < 0 (stream-K; only for the additive RESID epilogue, whose partial
+//  splits == -1 (stream-K; only for the additive RESID epilogue, whose partial
 //    products are reduce-added into x): group g owns the contiguous range
 //    [g * L, (g + 1) * L) of all tiles' k-blocks taken in tile order,
 //    L = ceil(tiles * k_blocks / groups), so every group does the same number
 //    of k-blocks; its units are the pieces of that range inside each tile.
+//  splits == -2 (tail split; also additive RESID only): the first
+//    floor(tiles / groups) * groups tiles are dealt whole, round-robin; the
+//    k-blocks of the remaining tiles are spread as in stream-K with spans of
+//    L = max(TAIL_MIN_SPAN, ceil(tail k-blocks / groups)) (fewer groups take
+//    part when the tail is short), so the last, partial round of whole tiles
+//    becomes a short round in which every group works.
 struct Units {
-  int grp0, ngrp, num_tiles, k_blocks, splits, kpb;
+  int grp0, ngrp, num_tiles, k_blocks, splits, kpb, full;
   long lo, hi;
-  __device__ Units(int g, int ng, int nt, int kb, int sp)
-      : grp0(g), ngrp(ng), num_tiles(nt), k_blocks(kb), splits(sp), kpb(0), lo(0), hi(0) {
+  __device__ Units(int g, int ng, int nt, int kb, int sp, int min_span)
+      : grp0(g), ngrp(ng), num_tiles(nt), k_blocks(kb), splits(sp), kpb(0), full(0), lo(0), hi(0) {
     if (sp > 0) {
       kpb = (kb + sp - 1) / sp;
     } else {
-      const long total = (long)nt * kb;
-      const long L = (total + ng - 1) / ng;
+      full = sp == -2 ? (nt / ng) * ng : 0;
+      const long total = (long)(nt - full) * kb;
+      const long L = max(sp == -2 ? (long)min_span : 1L, (total + ng - 1) / ng);
       lo = min(total, (long)g * L);
       hi = min(total, lo + L);
     }
@@ -129,12 +139,21 @@ struct Units {
       kb1 = min(k_blocks, kb0 + kpb);
       return true;
     }
+    const int nwhole = full / ngrp;
+    if (i < nwhole) {
+      t = grp0 + i * ngrp;
+      kb0 = 0;
+      kb1 = k_blocks;
+      return true;
+    }
+    i -= nwhole;
     if (lo >= hi) return false;
-    t = (int)(lo / k_blocks) + i;
-    const long s = max(lo, (long)t * k_blocks), e = min(hi, (long)(t + 1) * k_blocks);
+    const int tt = (int)(lo / k_blocks) + i;
+    const long s = max(lo, (long)tt * k_blocks), e = min(hi, (long)(tt + 1) * k_blocks);
     if (s >= e) return false;
-    kb0 = (int)(s - (long)t * k_blocks);
-    kb1 = (int)(e - (long)t * k_blocks);
+    t = full + tt;
+    kb0 = (int)(s - (long)tt * k_blocks);
+    kb1 = (int)(e - (long)tt * k_blocks);
     return true;
   }
 };
@@ -171,7 +190,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int num_tiles = m_tiles * n_tiles;
   const int k_blocks = (K + BK - 1) / BK;
   // work units: see Units (splits != 1 only for the additive RESID epilogue)
-  const Units units(grp0, ngrp, num_tiles, k_blocks, splits);
+  const Units units(grp0, ngrp, num_tiles, k_blocks, splits, TAIL_MIN_SPAN);
 
   auto full = [&](int s) { return smem_u32(&bars[s]); };
   auto empty = [&](int s) { return smem_u32(&bars[STAGES + s]); };
@@ -628,6 +647,23 @@ double wave_eff(long units, int sms) {
   return waves ? (double)units / (double)(waves * sms) : 0.0;
 }
 
+// Tail split (Units, splits == -2) of a residual GEMM: k-block time per group
+// of whole tiles, (full rounds + 1) * kb, against full rounds * kb + the tail
+// span + one k-block for the extra accumulator hand-off; taken at a predicted
+// gain above 3 %.  Measured (CUDA events, the DiT layer GEMMs): W2 -2.9 % at
+// 54,504 rows and -1.9 % at 27,252 (the config-4 steps), Wo within 1 %; W2 at
+// 6,800 rows (a predicted 2 % gain) ran 3 % slower and stays on whole tiles.
+// force: take it wherever some tile would be shared (tests).
+bool tail_split_pays(long tiles, int groups, int kb, bool force) {
+  const long full_rounds = tiles / groups, tail = tiles - full_rounds * groups;
+  if (tail == 0) return false;
+  const long span = std::max<long>(TAIL_MIN_SPAN, (tail * kb + groups - 1) / groups);
+  if (span >= kb) return false;  // no tile would be shared
+  const double whole = (double)(full_rounds + 1) * kb;
+  const double split = (double)full_rounds * kb + span + 1.0;
+  return force || split < 0.97 * whole;
+}
+
 }  // namespace tc
 
 // bf16 2-D tensor map with a {64, box_rows} box and 128-byte swizzle (cached).
@@ -682,6 +718,14 @@ void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int
       }
     }
     if (splits == 1 && eff1 < 0.8 && kb >= 64 && tiles * kb >= 8L * sms) splits = -1;
+    // Otherwise a tail split when the last wave is partly empty (by TMA
+    // reduce-add only: the read-modify-write path is not additive).
+    // IRT_TAIL_SPLIT=0 turns it off, =1 takes it wherever a tile is shared.
+    const char* ts = std::getenv("IRT_TAIL_SPLIT");
+    const bool ts_off = ts && ts[0] == '0', ts_force = ts && ts[0] == '1';
+    const bool xtma_ok = p.x && (N % 32) == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 &&
+                         (!p.gate || (reinterpret_cast<uintptr_t>(p.gate) & 15) == 0);
+    if (splits == 1 && xtma_ok && !ts_off && tc::tail_split_pays(tiles, sms, kb, ts_force)) splits = -2;
   }
   if (pairs) {
     if (use256) tc::launch<256, 2>(A, lda, B, ldb, M, N, K, splits, p, s);

@@ -271,3 +271,25 @@ def test_attention_key_mask_and_empty_rows(dev, bf16, path):
     ref = _attn_ref(q, k, torch.nan_to_num(v), None, None, None, mask, seqs[:1], H, hd)
     err = (out[:64].float() - ref[:64]).abs().max().item() / ref[:64].abs().max().item()
     assert err < (2e-2 if bf16 else 1e-5), f"rel err {err}"
+
+
+@pytest.mark.parametrize("force", ["1", None])
+@pytest.mark.parametrize("M,K", [(54504, 2048), (27252, 5888), (6800, 5888), (1000, 1024)])
+def test_gemm_resid_tail_split(dev, monkeypatch, force, M, K):
+    """Residual GEMMs whose last wave of whole tiles is partly empty run the
+    full rounds on whole tiles and spread the tail tiles' k-blocks over every
+    SM pair (pieces reduce-added into x); forced on (IRT_TAIL_SPLIT=1) and as
+    chosen by the dispatch rule."""
+    if force:
+        monkeypatch.setenv("IRT_TAIL_SPLIT", force)
+    N = 2048
+    g = torch.Generator(device=dev).manual_seed(M + K + 1)
+    A = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    W = (torch.randn(N, K, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    x = torch.randn(M, N, device=dev, generator=g)
+    gate = torch.randn(N, device=dev, generator=g)
+    ref = x + gate * (A.float() @ W.float().T)
+    check(hooks().irtt_gemm_epi(2, ptr(A), ptr(W), M, N, K, 0, None, None, None, None, None, None, None, None,
+                                None, 0, 0, 0, ptr(x), ptr(gate), 0))
+    err = (x - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-5, f"tail-split resid rel err {err}"
