@@ -613,6 +613,8 @@ def main():
     ap.add_argument("--codec-only", action="store_true",
                     help="time the config-5 DACVAE decode alone (16 utterances, seeded latents)")
     ap.add_argument("--codec-precision", default="bf16", choices=["bf16", "f32"])
+    ap.add_argument("--codec-utts", type=int, default=16,
+                    help="with --codec-only: decode the first N of the 16 config-5 utterances (profiling case)")
     ap.add_argument("--attn-case", nargs="?", const="c3", default=None, choices=["c3", "c3p", "c4", "c4p"],
                     help="only the joint attention of one layer: config-3 CFG step (c3), config-4 CFG step (c4) "
                          "or config-4 plain step (c4p), --steps launches (profiling case)")
@@ -887,7 +889,7 @@ def codec_only(args):
     import torch
     pkg = load_pkg()
     import irodori_b200.synth as synth
-    utts = synth.throughput_utterances(16, seed=5)
+    utts = synth.throughput_utterances(16, seed=5)[:max(1, args.codec_utts)]
     lens = [u[1] for u in utts]
     T = max(lens)
     path = Path(tempfile.gettempdir()) / "irodori_bench" / "codec_ref_init_r0.safetensors"
@@ -895,8 +897,8 @@ def codec_only(args):
     if not path.exists():
         synth.make_codec_checkpoint(str(path), seed=5, width_div=1, init="reference")
     codec = pkg.load_codec(str(path), device=0, precision=args.codec_precision)
-    lat = torch.randn(16, T, 32, generator=torch.Generator().manual_seed(5)).cuda()
-    wav = torch.empty(16, 1, T * codec.hop_length(), device="cuda")
+    lat = torch.randn(len(lens), T, 32, generator=torch.Generator().manual_seed(5)).cuda()
+    wav = torch.empty(len(lens), 1, T * codec.hop_length(), device="cuda")
     for _ in range(args.warmup):
         codec.decode(lat, out=wav, lengths=lens)
     torch.cuda.synchronize()

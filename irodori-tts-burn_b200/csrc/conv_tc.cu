@@ -167,14 +167,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t d_tmem = tmem_base + buf * C::ACC_STRIDE;
         for (int kb = 0; kb < kbs; ++kb, ++it) {
           const int s = it % STAGES;
+          // input channels past cin are zero padding (the TMA zero fill times
+          // zero weights): the last k-block of a tap issues only the MMAs that
+          // cover real channels (96 channels: 2 of 4 in the second block)
+          const int c0 = (kb % kpt) * BK;
+          const int nkk = min(BK / 16, (a.cin - c0 + 15) / 16);
           mbar_wait(full(s), (it / STAGES) & 1);
           tc_fence_after();
           const uint32_t a_addr = smem_u32(tiles + s * C::STAGE_BYTES);
           const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            umma_f16(d_tmem, sdesc_kmajor(a_addr + kk * 32), sdesc_kmajor(b_addr + kk * 32), C::IDESC,
-                     (kb | kk) ? 1u : 0u);
+            if (kk < nkk)
+              umma_f16(d_tmem, sdesc_kmajor(a_addr + kk * 32), sdesc_kmajor(b_addr + kk * 32), C::IDESC,
+                       (kb | kk) ? 1u : 0u);
           umma_commit(empty(s));  // frees the stage when these MMAs complete
         }
         umma_commit(tfull(buf));  // accumulator ready
@@ -202,6 +208,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool valid = ok && a.frame_src[o / a.out_scale] >= 0;
       const unsigned okm = __ballot_sync(0xffffffffu, ok);
       const unsigned vm = __ballot_sync(0xffffffffu, valid);
+      const long rstep = (long)ostride * a.cout;
+      // The residual rows (1x1 convolutions) do not depend on this unit's
+      // MMAs: the first column chunk is loaded before the accumulator wait,
+      // and each next chunk while the current one is finished, so the loads'
+      // latency hides behind the MMAs and the stores.
+      auto load_x = [&](int c, float(&dst)[32]) {
+        const long b = (long)o0 * a.cout + n0 + c + lane;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) dst[i] = ((okm >> i) & 1) ? a.x[b + i * rstep] : 0.f;
+      };
+      float xv[32];
+      if (a.add_res && 32 * half < BN) load_x(32 * half, xv);
       mbar_wait(tfull(buf), (tl >> 1) & 1);
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * C::ACC_STRIDE;
@@ -209,6 +227,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int c = 32 * half; c < BN; c += 64) {
         uint32_t r[32];
         tmem_ld32(taddr + c, r);
+        const bool more = a.add_res && c + 64 < BN;
+        float xn[32];
+        if (more) load_x(c + 64, xn);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) stg[lane * 33 + i] = __uint_as_float(r[i]);
@@ -221,13 +242,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           inv = 1.f / (al + 1e-9f);
         }
         const long col = co;
-        const long rstep = (long)ostride * a.cout;
         const long base = (long)o0 * a.cout + col;
-        float xv[32];
-        if (a.add_res) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) xv[i] = ((okm >> i) & 1) ? a.x[base + i * rstep] : 0.f;
-        }
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           if (!((okm >> i) & 1)) continue;
@@ -237,6 +252,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           const long idx = base + i * rstep;
           if (a.x) a.x[idx] = v;
           if (a.p) a.p[idx] = __float2bfloat16_rn(a.alpha ? snake_inv(v, al, inv) : v);
+        }
+        if (more) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) xv[i] = xn[i];
         }
         __syncwarp();
       }
@@ -269,39 +288,49 @@ __global__ void pack_latent_kernel(const float* __restrict__ lat, const int* __r
 }
 
 // Head conv (src/codec/decoder.rs:43-54): wav = tanh(conv_k(Snake(x))) with the
-// Snake already applied by the producer of `x` (bf16 rows [R, C]).  One thread
-// per output row; rows of gap frames are skipped, utterance rows go to
+// Snake already applied by the producer of `x` (bf16 rows [R, C]).  One block
+// of HEAD_ROWS threads per HEAD_ROWS output rows: the (HEAD_ROWS + K - 1)
+// input rows the block needs are staged in shared memory with coalesced
+// 4-byte loads (row pitch C/2 + 1 words, odd, so the 32 lanes of a warp --
+// 32 consecutive rows -- read 32 different banks), then each thread computes
+// its row in the same operation order as a per-row loop over (tap, channel).
+// Rows of gap frames are skipped; utterance rows go to
 // wav[src * hop + (row % hop)].
+constexpr int HEAD_ROWS = 128;
 template <int C>
-__global__ void __launch_bounds__(256) head_kernel(const __nv_bfloat16* __restrict__ x, int R,
-                                                   const float* __restrict__ w, const float* __restrict__ bias, int K,
-                                                   int pad, const int* __restrict__ frame_src, int hop,
-                                                   float* __restrict__ wav) {
+__global__ void __launch_bounds__(HEAD_ROWS) head_kernel(const __nv_bfloat16* __restrict__ x, int R,
+                                                         const float* __restrict__ w,
+                                                         const float* __restrict__ bias, int K, int pad,
+                                                         const int* __restrict__ frame_src, int hop,
+                                                         float* __restrict__ wav) {
+  constexpr int W2 = C / 2, PITCH = W2 + 1, ROWS = HEAD_ROWS + 6;
   __shared__ float ws[7 * C];
-  for (int i = threadIdx.x; i < K * C; i += blockDim.x) {
+  __shared__ uint32_t xs[ROWS * PITCH];
+  for (int i = threadIdx.x; i < K * C; i += HEAD_ROWS) {
     const int k = i / C, c = i % C;
     ws[i] = w[(long)c * K + k];  // weight [1, C, K]
   }
+  const int o0 = blockIdx.x * HEAD_ROWS;
+  const int r0 = o0 - pad;  // first staged input row
+  const uint32_t* xw = reinterpret_cast<const uint32_t*>(x);
+  for (int i = threadIdx.x; i < (HEAD_ROWS + K - 1) * W2; i += HEAD_ROWS) {
+    const int rr = i / W2, j = i - rr * W2;
+    const int t = r0 + rr;
+    xs[rr * PITCH + j] = (t >= 0 && t < R) ? xw[(long)t * W2 + j] : 0u;
+  }
   __syncthreads();
-  const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  const int o = o0 + threadIdx.x;
   if (o >= R) return;
   const int src = frame_src[o / hop];
   if (src < 0) return;
   float acc = bias ? bias[0] : 0.f;
   for (int k = 0; k < K; ++k) {
-    const int t = o + k - pad;
-    if (t < 0 || t >= R) continue;
-    const uint4* row = reinterpret_cast<const uint4*>(x + (long)t * C);
+    const uint32_t* row = xs + (threadIdx.x + k) * PITCH;
 #pragma unroll
-    for (int v = 0; v < C / 8; ++v) {
-      const uint4 u = row[v];
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(h[j]);
-        acc = fmaf(f.x, ws[k * C + v * 8 + 2 * j], acc);
-        acc = fmaf(f.y, ws[k * C + v * 8 + 2 * j + 1], acc);
-      }
+    for (int j = 0; j < W2; ++j) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(row + j));
+      acc = fmaf(f.x, ws[k * C + 2 * j], acc);
+      acc = fmaf(f.y, ws[k * C + 2 * j + 1], acc);
     }
   }
   wav[(long)src * hop + (o % hop)] = tanhf(acc);
@@ -382,12 +411,13 @@ void pack_latent_rows(const float* lat, const int* frame_src, bf16* out, int F, 
 void codec_head_rows(const bf16* x, int R, int C, const float* w, const float* bias, int K, int pad,
                      const int* frame_src, int hop, float* wav, cudaStream_t s) {
   if (K > 7) throw unsupported("codec head kernel > 7");
-  const unsigned grid = (unsigned)((R + 255) / 256);
+  const unsigned grid = (unsigned)((R + ctc::HEAD_ROWS - 1) / ctc::HEAD_ROWS);
+  const int nt = ctc::HEAD_ROWS;
   switch (C) {
-    case 96: ctc::head_kernel<96><<<grid, 256, 0, s>>>(x, R, w, bias, K, pad, frame_src, hop, wav); break;
-    case 64: ctc::head_kernel<64><<<grid, 256, 0, s>>>(x, R, w, bias, K, pad, frame_src, hop, wav); break;
-    case 128: ctc::head_kernel<128><<<grid, 256, 0, s>>>(x, R, w, bias, K, pad, frame_src, hop, wav); break;
-    case 32: ctc::head_kernel<32><<<grid, 256, 0, s>>>(x, R, w, bias, K, pad, frame_src, hop, wav); break;
+    case 96: ctc::head_kernel<96><<<grid, nt, 0, s>>>(x, R, w, bias, K, pad, frame_src, hop, wav); break;
+    case 64: ctc::head_kernel<64><<<grid, nt, 0, s>>>(x, R, w, bias, K, pad, frame_src, hop, wav); break;
+    case 128: ctc::head_kernel<128><<<grid, nt, 0, s>>>(x, R, w, bias, K, pad, frame_src, hop, wav); break;
+    case 32: ctc::head_kernel<32><<<grid, nt, 0, s>>>(x, R, w, bias, K, pad, frame_src, hop, wav); break;
     default: throw unsupported("codec head: channels must be 32, 64, 96 or 128");
   }
   IRT_CHECK_LAUNCH();
