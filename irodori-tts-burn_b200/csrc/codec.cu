@@ -272,6 +272,13 @@ Codec::Codec(int dev, const std::string& path, int precision) : device(dev), pre
   IRT_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   SafeTensorsFile st(path);
   auto get = [&](const std::string& k, size_t rank) -> const TensorView& { return st.get(k, rank); };
+  // 1 / (alpha + 1e-9) in f32, the Snake epilogue's reciprocal (a correctly
+  // rounded divide, as the kernels would compute it)
+  auto add_inv = [&](const DevBuf& alpha, const std::vector<float>& h) {
+    std::vector<float> inv(h.size());
+    for (size_t i = 0; i < h.size(); ++i) inv[i] = 1.0f / (h[i] + 1e-9f);
+    up_host(snake_inv[alpha.p], inv);
+  };
   auto conv = [&](Conv& c, const std::string& p, int dil) {
     std::vector<long> shp;
     std::vector<float> h = conv_weight(st, p, shp);
@@ -294,7 +301,7 @@ Codec::Codec(int dev, const std::string& path, int precision) : device(dev), pre
     Block& bl = blocks[i];
     std::string p = "decoder.model." + std::to_string(i + 1);
     bl.stride = rates[i];
-    up_f32(bl.alpha, get(p + ".block.0.alpha", 3));
+    add_inv(bl.alpha, up_f32(bl.alpha, get(p + ".block.0.alpha", 3)));
     std::vector<long> shp;
     std::vector<float> h = conv_weight(st, p + ".block.1", shp);  // [cin, cout, 2s]
     bl.ct.cin = (int)shp[0];
@@ -312,13 +319,13 @@ Codec::Codec(int dev, const std::string& path, int precision) : device(dev), pre
     const int ids[3] = {4, 5, 8}, dils[3] = {1, 3, 9};
     for (int r = 0; r < 3; ++r) {
       std::string q = p + ".block." + std::to_string(ids[r]);
-      up_f32(bl.res[r].a0, get(q + ".block.0.alpha", 3));
+      add_inv(bl.res[r].a0, up_f32(bl.res[r].a0, get(q + ".block.0.alpha", 3)));
       conv(bl.res[r].c1, q + ".block.1", dils[r]);
-      up_f32(bl.res[r].a2, get(q + ".block.2.alpha", 3));
+      add_inv(bl.res[r].a2, up_f32(bl.res[r].a2, get(q + ".block.2.alpha", 3)));
       conv(bl.res[r].c3, q + ".block.3", 1);
     }
   }
-  up_f32(head_alpha, get("decoder.wm_model.encoder_block.pre.0.alpha", 3));
+  add_inv(head_alpha, up_f32(head_alpha, get("decoder.wm_model.encoder_block.pre.0.alpha", 3)));
   conv(head, "decoder.wm_model.encoder_block.pre.1", 1);
   if (qout.cin != 32) throw shape_error("quantizer.out_proj expects 32 latent channels");
   // bf16 mode runs on the tensor-core path when every layer fits its tiling
@@ -334,6 +341,13 @@ Codec::Codec(int dev, const std::string& path, int precision) : device(dev), pre
     tc = ok;
   }
   codec_noalloc_prepare();
+}
+
+const float* Codec::inv_of(const float* alpha) const {
+  if (!alpha) return nullptr;
+  auto it = snake_inv.find(alpha);
+  if (it == snake_inv.end()) throw Error(IRT_E_INVALID_ARG, "codec: Snake alpha without its reciprocal table");
+  return it->second.as<float>();
 }
 
 Codec::~Codec() {
@@ -503,6 +517,7 @@ void Codec::decode_tc(const float* lat, int B, int T, const int* lengths, float*
       a.frame_src = fsrc;
       a.bias = c.b.p ? c.b.as<float>() : nullptr;
       a.alpha = alpha;
+      a.alpha_inv = inv_of(alpha);
       a.x = x;
       a.add_res = add_res;
       a.p = oth;

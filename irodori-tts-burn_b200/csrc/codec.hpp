@@ -1,6 +1,7 @@
 // DACVAE decoder object (src/codec/model.rs:18-65).
 #pragma once
 
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -22,6 +23,7 @@ struct ConvTcArgs {
   const int* frame_src = nullptr;  // per latent frame: utterance frame index, or -1 for a gap
   const float* bias = nullptr;
   const float* alpha = nullptr;    // Snake alpha applied to the bf16 output (nullptr: identity)
+  const float* alpha_inv = nullptr;  // 1 / (alpha + 1e-9) per channel (with alpha)
   float* x = nullptr;              // f32 output rows [rows_out, cout] (nullptr: not written)
   int add_res = 0;                 // x = x + conv (residual, in place)
   bf16* p = nullptr;               // bf16 output rows [rows_out, cout] (nullptr: not written)
@@ -58,6 +60,10 @@ struct Codec {
   Conv qout, stem, head;
   Block blocks[4];
   DevBuf head_alpha;
+  // 1 / (alpha + 1e-9) of every Snake alpha above, keyed by the alpha buffer
+  // (the tensor-core epilogue multiplies instead of dividing per element)
+  std::map<const void*, DevBuf> snake_inv;
+  const float* inv_of(const float* alpha) const;
   DevBuf in, buf0, buf1, buf2;
   // bf16 tensor-core path: row buffers and the frame table
   bool tc = false;

@@ -42,6 +42,8 @@ namespace irt {
 
 // bf16 2-D tensor map, {64, box_rows} box, 128-byte swizzle (gemm_tc.cu).
 const CUtensorMap& tma_map_bf16(const void* p, long rows, long cols, long ld, int box_rows);
+// {32, 32} boxes: f32 with the 128-byte swizzle or bf16 with the 64-byte swizzle (gemm_tc.cu).
+CUtensorMap tma_map_tile32(const void* p, bool f32, long rows, long cols, long ld);
 
 namespace ctc {
 
@@ -52,17 +54,32 @@ using namespace tcx;
 constexpr int BM = 128, BK = 64, EPI_WARPS = 8, THREADS = 64 + 32 * EPI_WARPS;
 constexpr uint32_t A_BYTES = BM * BK * 2;
 
+// Per epilogue warp: a 32 x 33 f32 transpose buffer (ConvTranspose path), or
+// the staging tiles of the stride-1 path -- 32 x 32 f32 (128-byte rows,
+// 128-byte swizzle) then 32 x 32 bf16 (64-byte rows, 64-byte swizzle), both
+// stored by TMA.  6 KB keeps every f32 tile 1024-byte aligned.  (A second
+// set per warp, so that one chunk's stores drain while the next is computed,
+// measured no faster and cost the 192-wide layers a pipeline stage.)
+constexpr uint32_t EPI_SET = 6144;
+
 template <int BN>
 struct Cfg {
+  static constexpr uint32_t EPI_SLOT = EPI_SET;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (184 * 1024) / STAGE_BYTES > 8 ? 8 : (184 * 1024) / STAGE_BYTES;
+  static constexpr uint32_t STAGE_BUDGET = 176 * 1024;
+  static constexpr int STAGES = STAGE_BUDGET / STAGE_BYTES > 8 ? 8 : STAGE_BUDGET / STAGE_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
   // second accumulator at a power-of-two column offset
   static constexpr uint32_t ACC_STRIDE = TMEM_COLS / 2;
-  // alignment slack | stages | barriers (256 B) | one 32x33 f32 transpose buffer per epilogue warp
-  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256 + EPI_WARPS * 32 * 33 * 4;
+  // alignment slack | stages | epilogue slots (1024-aligned) | barriers (256 B)
+  static constexpr uint32_t OFF_EPI = STAGES * STAGE_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_EPI + EPI_WARPS * EPI_SLOT;
+  static_assert(STAGES >= 3, "at least three pipeline stages");
+  static constexpr size_t SMEM = 1024 + (size_t)OFF_BAR + 256;
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN);
+  static_assert((OFF_EPI % 1024) == 0, "epilogue slots must be 1024-byte aligned");
+  static_assert(32 * 33 * 4 <= EPI_SET, "transpose buffer fits a slot");
 };
 
 // A-operand row offset of tap `tap` for output phase `phase`.
@@ -72,6 +89,11 @@ __device__ __forceinline__ int a_row_off(const ConvTcArgs& a, int phase, int tap
 // Output row of GEMM row q in phase `phase`.
 __device__ __forceinline__ int out_row(const ConvTcArgs& a, int phase, int q) {
   return a.convt ? (q + (phase < a.pad ? 1 : 0)) * a.stride + phase - a.pad : q;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&t);
 }
 
 // Snake with a precomputed 1 / (alpha + 1e-9); the hardware sine (MUFU) is
@@ -84,15 +106,16 @@ __device__ __forceinline__ float snake_inv(float v, float al, float inv) {
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmP,
                    const __grid_constant__ ConvTcArgs a) {
   using C = Cfg<BN>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
-  float* stage_f = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES + 256);
+  uint8_t* epi = smem + C::OFF_EPI;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int m_tiles = (a.rows_in + BM - 1) / BM, n_tiles = a.cout / BN;
@@ -190,7 +213,110 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- epilogue warps 2 .. 2 + EPI_WARPS ----------------
     const int quad = warp & 3;              // TMEM lane quadrant this warp may access
     const int half = (warp - 2) / 4;        // which 32-column chunks it takes
-    float* stg = stage_f + (warp - 2) * (32 * 33);
+    uint8_t* slot = epi + (warp - 2) * C::EPI_SLOT;
+    if (!a.convt) {
+      // Stride-1 convolutions (output row = GEMM row): thread = output row.
+      // Each 32 x 32 chunk leaves through this warp's staging tiles by TMA
+      // stores (f32 residual stream, bf16 Snake output); the residual rows
+      // are read straight into registers (a float4 per 4 columns), the first
+      // chunk before the accumulator wait and each next one while the current
+      // one is finished.  Gap rows are written as exact zeros.
+      uint32_t tl = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x, ++tl) {
+        int mi, ph, ni;
+        unit_coords(u, mi, ph, ni);
+        const int m0 = mi * BM, n0 = ni * BN;
+        const int buf = tl & 1;
+        const int q0 = m0 + quad * 32;
+        const int row = q0 + lane;
+        const bool ok = row < a.rows_in;
+        const bool valid = ok && a.frame_src[row / a.out_scale] >= 0;
+        const float* xrow = a.x + (long)(ok ? row : 0) * a.cout + n0;
+        auto load_x = [&](int c, float4(&d)[8]) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            d[k] = ok ? reinterpret_cast<const float4*>(xrow + c)[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+        };
+        float4 xv[8];
+        if (a.add_res && 32 * half < BN) load_x(32 * half, xv);
+        mbar_wait(tfull(buf), (tl >> 1) & 1);
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * C::ACC_STRIDE;
+#pragma unroll 1
+        for (int c = 32 * half; c < BN; c += 64) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c, r);
+          const bool more = a.add_res && c + 64 < BN;
+          float4 xn[8];
+          if (more) load_x(c + 64, xn);
+          tmem_wait_ld();
+          // the staging tiles: the previous chunk's stores have read them
+          uint8_t* xs = slot;         // f32 [32][32], 128-byte swizzle
+          uint8_t* ps = slot + 4096;  // bf16 [32][32], 64-byte swizzle
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          const float* bp = a.bias ? a.bias + n0 + c : nullptr;
+          const float* ap = a.alpha ? a.alpha + n0 + c : nullptr;
+          const float* ip = a.alpha ? a.alpha_inv + n0 + c : nullptr;
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {  // 8 columns: one 16-byte chunk of the bf16 row
+            float v[8];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int k = 2 * m + h;  // float4 group: columns 4k .. 4k + 3
+              const float4 b4 = bp ? reinterpret_cast<const float4*>(bp)[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+              float w0 = __uint_as_float(r[4 * k]) + b4.x, w1 = __uint_as_float(r[4 * k + 1]) + b4.y;
+              float w2 = __uint_as_float(r[4 * k + 2]) + b4.z, w3 = __uint_as_float(r[4 * k + 3]) + b4.w;
+              if (a.add_res) {
+                w0 += xv[k].x;
+                w1 += xv[k].y;
+                w2 += xv[k].z;
+                w3 += xv[k].w;
+              }
+              if (!valid) w0 = w1 = w2 = w3 = 0.f;
+              if (a.x)
+                *reinterpret_cast<float4*>(xs + lane * 128 + ((k ^ (lane & 7)) << 4)) = make_float4(w0, w1, w2, w3);
+              if (ap) {
+                const float4 al = reinterpret_cast<const float4*>(ap)[k];
+                const float4 in = reinterpret_cast<const float4*>(ip)[k];
+                w0 = snake_inv(w0, al.x, in.x);
+                w1 = snake_inv(w1, al.y, in.y);
+                w2 = snake_inv(w2, al.z, in.z);
+                w3 = snake_inv(w3, al.w, in.w);
+              }
+              v[4 * h] = w0;
+              v[4 * h + 1] = w1;
+              v[4 * h + 2] = w2;
+              v[4 * h + 3] = w3;
+            }
+            if (a.p) {
+              uint4 pk;
+              pk.x = pack_bf16x2(v[0], v[1]);
+              pk.y = pack_bf16x2(v[2], v[3]);
+              pk.z = pack_bf16x2(v[4], v[5]);
+              pk.w = pack_bf16x2(v[6], v[7]);
+              *reinterpret_cast<uint4*>(ps + lane * 64 + ((m ^ ((lane >> 1) & 3)) << 4)) = pk;
+            }
+          }
+          fence_proxy_async();  // generic-proxy smem writes -> visible to the TMA stores
+          __syncwarp();
+          if (lane == 0 && q0 < a.rows_out) {  // rows past the end are clipped by the TMA unit
+            if (a.x) tma_store_2d(&tmX, smem_u32(xs), n0 + c, q0);
+            if (a.p) tma_store_2d(&tmP, smem_u32(ps), n0 + c, q0);
+            bulk_commit();
+          }
+          if (more) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) xv[k] = xn[k];
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty(buf));
+      }
+      if (lane == 0) bulk_wait0();  // every store of this warp has completed
+    } else {
+    float* stg = reinterpret_cast<float*>(slot);
     const int ostride = a.convt ? a.stride : 1;
     uint32_t tl = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++tl) {
@@ -262,6 +388,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty(buf));
+    }
     }
   }
 
@@ -371,7 +498,11 @@ void launch(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) 
   const CUtensorMap tb = tma_map_bf16(w, (long)a.phases * a.cout, kcols, kcols, BN);
   const long units = (long)((a.rows_in + BM - 1) / BM) * a.phases * (a.cout / BN);
   const int grid = (int)std::min<long>(units, num_sms());
-  launch_pdl(conv_tc_kernel<BN>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, a);
+  // stride-1 path: TMA maps of the outputs (32 x 32 staging tiles); unused
+  // (any valid map) for ConvTranspose
+  const CUtensorMap tx = (!a.convt && a.x) ? tma_map_tile32(a.x, true, a.rows_out, a.cout, a.cout) : ta;
+  const CUtensorMap tp = (!a.convt && a.p) ? tma_map_tile32(a.p, false, a.rows_out, a.cout, a.cout) : ta;
+  launch_pdl(conv_tc_kernel<BN>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, tx, tp, a);
   IRT_CHECK_LAUNCH();
 }
 
@@ -388,6 +519,11 @@ void conv_tc(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s)
     throw unsupported("conv_tc: input must have >= 128 rows and >= 64 channels (multiple of 8)");
   if ((reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
     throw unsupported("conv_tc: operands must be 16-byte aligned");
+  if (a.alpha && !a.alpha_inv) throw Error(IRT_E_INVALID_ARG, "conv_tc: Snake alpha needs its reciprocal table");
+  if ((a.x && (reinterpret_cast<uintptr_t>(a.x) & 15)) || (a.p && (reinterpret_cast<uintptr_t>(a.p) & 15)) ||
+      (a.bias && (reinterpret_cast<uintptr_t>(a.bias) & 15)) ||
+      (a.alpha && ((reinterpret_cast<uintptr_t>(a.alpha) | reinterpret_cast<uintptr_t>(a.alpha_inv)) & 15)))
+    throw unsupported("conv_tc: outputs, bias and alpha must be 16-byte aligned");
   if ((long)a.rows_out * a.cout >= (1L << 31) || (long)a.rows_in * a.phases >= (1L << 31))
     throw unsupported("conv_tc: level too large for 32-bit row indices");
   switch (conv_tc_bn(a.cout)) {

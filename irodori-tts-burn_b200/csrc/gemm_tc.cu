@@ -666,6 +666,23 @@ bool tail_split_pays(long tiles, int groups, int kb, bool force) {
 
 }  // namespace tc
 
+// 2-D tensor map of {32, 32}-element boxes for epilogue staging tiles: f32
+// rows of 128 bytes with the 128-byte swizzle, or bf16 rows of 64 bytes with
+// the 64-byte swizzle.
+CUtensorMap tma_map_tile32(const void* p, bool f32, long rows, long cols, long ld) {
+  CUtensorMap m;
+  cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t gstride[1] = {(cuuint64_t)ld * (f32 ? 4 : 2)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = tc::get_encode()(&m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                                const_cast<void*>(p), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error(IRT_E_CUDA, "cuTensorMapEncodeTiled (tile32) failed (" + std::to_string((int)r) + ")");
+  return m;
+}
+
 // bf16 2-D tensor map with a {64, box_rows} box and 128-byte swizzle (cached).
 const CUtensorMap& tma_map_bf16(const void* p, long rows, long cols, long ld, int box_rows) {
   return tc::tensor_map(p, rows, cols, ld, box_rows);

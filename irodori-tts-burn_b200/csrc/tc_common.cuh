@@ -161,6 +161,14 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_rank0), "r"(c0), "r"(c1)
       : "memory");
 }
+// TMA store of a shared-memory box into global memory, bulk-group completion
+// (elements of the box outside the tensor are not written).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
 // TMA reduce-add of a shared-memory box into global memory (f32 add performed
 // atomically by the memory system), bulk-group completion.
 __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {

@@ -230,6 +230,16 @@ IRTT_API int irtt_conv_tc(const void* in, int rows_in, int cin, const void* w, i
     a.frame_src = frame_src;
     a.bias = bias;
     a.alpha = alpha;
+    // 1 / (alpha + 1e-9) per channel, as the codec uploads it at load
+    irt::DevBuf inv;
+    if (alpha) {
+      std::vector<float> h(cout);
+      IRT_CUDA(cudaMemcpy(h.data(), alpha, (size_t)cout * 4, cudaMemcpyDeviceToHost));
+      for (auto& v : h) v = 1.0f / (v + 1e-9f);
+      inv.alloc((size_t)cout * 4);
+      IRT_CUDA(cudaMemcpy(inv.p, h.data(), (size_t)cout * 4, cudaMemcpyHostToDevice));
+      a.alpha_inv = inv.as<float>();
+    }
     a.x = x;
     a.add_res = add_res;
     a.p = reinterpret_cast<irt::bf16*>(p);
