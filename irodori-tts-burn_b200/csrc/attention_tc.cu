@@ -28,6 +28,7 @@
 // Keys past a sequence's end get -inf scores; a row with no valid key outputs
 // 0.  Output = (O / l) * sigmoid-gate, bf16.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.hpp"
 #include "kernels.hpp"
@@ -41,19 +42,30 @@ namespace {
 
 using namespace tcx;
 
-constexpr int QT = 128, KT = 64, HDIM = 128, SM_WARPS = 4, THREADS = 64 + 32 * SM_WARPS, NKV = 2;
+constexpr int QT = 128, HDIM = 128, SM_WARPS = 4, THREADS = 64 + 32 * SM_WARPS, NKV = 2;
 constexpr uint32_t Q_BYTES = QT * HDIM * 2;     // 32 KB (two 16 KB 64-column halves)
 constexpr uint32_t Q_HALF = Q_BYTES / 2;
-constexpr uint32_t TILE_BYTES = KT * HDIM * 2;  // 16 KB (two 8 KB 64-column halves)
-constexpr uint32_t HALF = TILE_BYTES / 2;
-// smem: Q | K ring | V ring | barriers
-constexpr uint32_t OFF_Q = 0, OFF_K = Q_BYTES, OFF_V = OFF_K + NKV * TILE_BYTES;
-constexpr uint32_t OFF_BAR = OFF_V + NKV * TILE_BYTES;
-constexpr size_t SMEM = OFF_BAR + 256 + 1024;
-constexpr uint32_t IDESC_S = idesc_bf16(128, KT, false);
 constexpr uint32_t IDESC_O = idesc_bf16(128, HDIM, true);
-constexpr uint32_t TM_S = 0, TM_O = 128, TM_COLS = 256;
 constexpr float RESCALE_LOG2 = 8.f;  // raise the running max only beyond 2^8 growth
+
+// Key-tile width variants.  KT = 64: two CTAs per SM (256 TMEM columns and
+// ~98 KB of shared memory each).  KT = 128: one CTA per SM with all 512 TMEM
+// columns (two 128-column score buffers and O) and twice the keys per
+// softmax / MMA round trip -- for launches with no more CTAs than SMs, where
+// a second CTA per SM would not exist anyway.
+template <int KT_>
+struct AttnCfg {
+  static constexpr int KT = KT_;
+  static constexpr uint32_t TILE_BYTES = KT * HDIM * 2;  // two 64-column halves
+  static constexpr uint32_t HALF = TILE_BYTES / 2;
+  // smem: Q | K ring | V ring | barriers
+  static constexpr uint32_t OFF_Q = 0, OFF_K = Q_BYTES, OFF_V = OFF_K + NKV * TILE_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_V + NKV * TILE_BYTES;
+  static constexpr size_t SMEM = OFF_BAR + 256 + 1024;
+  static constexpr uint32_t IDESC_S = idesc_bf16(128, KT, false);
+  static constexpr uint32_t TM_S = 0, TM_O = 2 * KT, TM_COLS = KT == 64 ? 256 : 512;
+  static constexpr int CTAS_PER_SM = KT == 64 ? 2 : 1;
+};
 
 struct TcAttnArgs {
   const SeqDesc* seqs;
@@ -91,10 +103,16 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&t);
 }
 
-__global__ void __launch_bounds__(THREADS, 2)
+template <int KT_>
+__global__ void __launch_bounds__(THREADS, AttnCfg<KT_>::CTAS_PER_SM)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmCK,
                    const __grid_constant__ CUtensorMap tmCV, const __grid_constant__ TcAttnArgs a) {
+  using C = AttnCfg<KT_>;
+  constexpr int KT = C::KT;
+  constexpr uint32_t TILE_BYTES = C::TILE_BYTES, HALF = C::HALF, OFF_Q = C::OFF_Q, OFF_K = C::OFF_K,
+                     OFF_V = C::OFF_V, OFF_BAR = C::OFF_BAR, IDESC_S = C::IDESC_S, TM_S = C::TM_S, TM_O = C::TM_O,
+                     TM_COLS = C::TM_COLS;
   pdl_wait();  // before any read of predecessor output, in every CTA
   pdl_trigger();
   const SeqDesc sd = a.seqs[blockIdx.z];
@@ -236,9 +254,10 @@ __global__ void __launch_bounds__(THREADS, 2)
       const int kvalid = (j < n_self ? sd.len - j * KT : sd.ctx_len - (j - n_self) * KT);  // valid keys in tile
       mbar_wait(S_FULL(b), (j >> 1) & 1);
       tc_fence_after();
-      uint32_t sr[64];
-      tmem_ld32(tmem + lane_off + TM_S + b * KT, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      tmem_ld32(tmem + lane_off + TM_S + b * KT + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      uint32_t sr[KT];
+#pragma unroll
+      for (int g = 0; g < KT / 32; ++g)
+        tmem_ld32(tmem + lane_off + TM_S + b * KT + 32 * g, *reinterpret_cast<uint32_t(*)[32]>(&sr[32 * g]));
       tmem_wait_ld();
       if (kvalid < KT) {
 #pragma unroll
@@ -281,17 +300,19 @@ __global__ void __launch_bounds__(THREADS, 2)
       }
       // P = 2^(s * scale - m) as packed bf16: keys 2c, 2c+1 in column c of
       // the S buffer (this thread's scores are all in registers already)
-      uint32_t pk[32];
+      uint32_t pk[KT / 2];
       float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
+      for (int c = 0; c < KT / 2; ++c) {
         const float p0 = ex2(fmaf(__uint_as_float(sr[2 * c]), a.scale_log2, nbase));
         const float p1 = ex2(fmaf(__uint_as_float(sr[2 * c + 1]), a.scale_log2, nbase));
         rs0 += p0;
         rs1 += p1;
         pk[c] = pack_bf16x2(p0, p1);
       }
-      tmem_st32(tmem + lane_off + TM_S + b * KT, pk);
+#pragma unroll
+      for (int g = 0; g < KT / 64; ++g)
+        tmem_st32(tmem + lane_off + TM_S + b * KT + 32 * g, *reinterpret_cast<uint32_t(*)[32]>(&pk[32 * g]));
       tmem_wait_st();
       l_run = l_run * corr + (rs0 + rs1);
       tc_fence_before();
@@ -350,18 +371,22 @@ bool attention_tc_supported(const AttnParams& p) {
                        reinterpret_cast<uintptr_t>(p.v) | reinterpret_cast<uintptr_t>(p.out) |
                        (p.gsig ? reinterpret_cast<uintptr_t>(p.gsig) : 0) |
                        (p.ck ? reinterpret_cast<uintptr_t>(p.ck) : 0) | (p.cv ? reinterpret_cast<uintptr_t>(p.cv) : 0);
-  // TMA boxes are 128 rows (Q) and 64 rows (K, V, context): keep
-  // every tensor at least one box tall
-  const bool ctx_ok = !(p.ck && p.cv) || p.ctx_rows == 0 || p.ctx_rows >= KT;
+  // TMA boxes are 128 rows (Q) and 64 rows (K, V, context; 128 for the
+  // 128-key variant, taken only when they fit): keep every tensor at least
+  // one box tall
+  const bool ctx_ok = !(p.ck && p.cv) || p.ctx_rows == 0 || p.ctx_rows >= 64;
   return (al & 15) == 0 && p.rows >= QT && ctx_ok;
 }
 
-void attention_tc(const AttnParams& p, cudaStream_t s) {
+namespace {
+template <int KT>
+void launch_attn(const AttnParams& p, cudaStream_t s) {
+  using C = AttnCfg<KT>;
   static unsigned attr_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_mask & (1u << (dev & 31)))) {
-    IRT_CUDA(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM));
+    IRT_CUDA(cudaFuncSetAttribute(attn_tc_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
     attr_mask |= 1u << (dev & 31);
   }
   const long D = (long)p.H * HDIM;
@@ -379,8 +404,25 @@ void attention_tc(const AttnParams& p, cudaStream_t s) {
   a.H = p.H;
   a.scale_log2 = p.scale * 1.4426950408889634f;
   dim3 grid((p.max_len + QT - 1) / QT, p.H, p.nseq);
-  launch_pdl(attn_tc_kernel, grid, dim3(THREADS), SMEM, s, mq, mk, mv, mck, mcv, a);
+  launch_pdl(attn_tc_kernel<KT>, grid, dim3(THREADS), C::SMEM, s, mq, mk, mv, mck, mcv, a);
   IRT_CHECK_LAUNCH();
+}
+}  // namespace
+
+void attention_tc(const AttnParams& p, cudaStream_t s) {
+  // 128-key tiles when the launch has no more CTAs than SMs (one CTA per SM
+  // either way) and every K / V tensor is at least one 128-row box tall;
+  // 64-key tiles at two CTAs per SM otherwise.  IRT_ATTN_KT=64 / 128 forces
+  // one (measurements).
+  int dev = 0, sms = 0;
+  IRT_CUDA(cudaGetDevice(&dev));
+  IRT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const long ctas = (long)((p.max_len + QT - 1) / QT) * p.H * p.nseq;
+  const bool tall = p.rows >= 128 && (!(p.ck && p.cv) || p.ctx_rows == 0 || p.ctx_rows >= 128);
+  bool wide = tall && ctas <= sms;
+  if (const char* e = std::getenv("IRT_ATTN_KT")) wide = tall && std::atoi(e) == 128;
+  if (wide) launch_attn<128>(p, s);
+  else launch_attn<64>(p, s);
 }
 
 int read_and_clear_attn_error() { return read_and_clear_flag(); }

@@ -218,10 +218,24 @@ __global__ void __launch_bounds__(THREADS, 1)
       // Stride-1 convolutions (output row = GEMM row): thread = output row.
       // Each 32 x 32 chunk leaves through this warp's staging tiles by TMA
       // stores (f32 residual stream, bf16 Snake output); the residual rows
-      // are read straight into registers (a float4 per 4 columns), the first
-      // chunk before the accumulator wait and each next one while the current
-      // one is finished.  Gap rows are written as exact zeros.
+      // are read straight into registers (a float4 per 4 columns) one chunk
+      // ahead: the next chunk of the unit while the current one is finished,
+      // and during a unit's last chunk the first chunk of the warp's next
+      // unit (which does not depend on any MMA), so a warp keeps two chunks of
+      // residual rows in flight.  Gap rows are written as exact zeros.
       uint32_t tl = 0;
+      // residual rows: this lane's row of unit u, columns n0 + c .. + 31
+      auto load_x = [&](int u, int c, float4(&d)[8]) {
+        int mi, ph, ni;
+        unit_coords(u, mi, ph, ni);
+        const int row = mi * BM + quad * 32 + lane;
+        const bool ok = row < a.rows_in;
+        const float4* src = reinterpret_cast<const float4*>(a.x + (long)(ok ? row : 0) * a.cout + ni * BN + c);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) d[k] = ok ? src[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+      };
+      float4 xv[8];
+      if (a.add_res && 32 * half < BN && (int)blockIdx.x < units) load_x(blockIdx.x, 32 * half, xv);
       for (int u = blockIdx.x; u < units; u += gridDim.x, ++tl) {
         int mi, ph, ni;
         unit_coords(u, mi, ph, ni);
@@ -231,14 +245,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int row = q0 + lane;
         const bool ok = row < a.rows_in;
         const bool valid = ok && a.frame_src[row / a.out_scale] >= 0;
-        const float* xrow = a.x + (long)(ok ? row : 0) * a.cout + n0;
-        auto load_x = [&](int c, float4(&d)[8]) {
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            d[k] = ok ? reinterpret_cast<const float4*>(xrow + c)[k] : make_float4(0.f, 0.f, 0.f, 0.f);
-        };
-        float4 xv[8];
-        if (a.add_res && 32 * half < BN) load_x(32 * half, xv);
         mbar_wait(tfull(buf), (tl >> 1) & 1);
         tc_fence_after();
         const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * C::ACC_STRIDE;
@@ -246,9 +252,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int c = 32 * half; c < BN; c += 64) {
           uint32_t r[32];
           tmem_ld32(taddr + c, r);
-          const bool more = a.add_res && c + 64 < BN;
+          // the residual chunk after this one: this unit's next, or the first
+          // of this warp's next unit
+          const bool in_unit = c + 64 < BN;
+          const bool more = a.add_res && (in_unit || u + (int)gridDim.x < units);
           float4 xn[8];
-          if (more) load_x(c + 64, xn);
+          if (more) load_x(in_unit ? u : u + (int)gridDim.x, in_unit ? c + 64 : 32 * half, xn);
           tmem_wait_ld();
           // the staging tiles: the previous chunk's stores have read them
           uint8_t* xs = slot;         // f32 [32][32], 128-byte swizzle

@@ -208,6 +208,15 @@ def _attn_ref(q, k, v, g, ck, cv, key_mask, seqs, H, hd):
 ATTN_PATHS = [(1, 0), (1, 1), (0, 2)]  # (bf16, path): tcgen05, mma.sync, SIMT
 
 
+@pytest.mark.parametrize("kt", ["64", "128"])
+@pytest.mark.parametrize("case", ["mixed", "config3", "ragged"])
+def test_attention_key_tile_variants(dev, monkeypatch, kt, case):
+    """Both key-tile widths of the tcgen05 kernel (64 keys at two CTAs per SM,
+    128 keys at one CTA per SM), forced through IRT_ATTN_KT."""
+    monkeypatch.setenv("IRT_ATTN_KT", kt)
+    test_attention_matches_torch(dev, 1, 0, case)
+
+
 @pytest.mark.parametrize("bf16,path", ATTN_PATHS)
 @pytest.mark.parametrize("case", ["mixed", "config3", "ragged"])
 def test_attention_matches_torch(dev, bf16, path, case):
