@@ -175,3 +175,43 @@ def test_device_buffers_and_errors(gpu, pkg, synth, tiny_ckpt, tmp_path):
     with pytest.raises(pkg.IrodoriError) as ei:
         pkg.InferenceBuilder(0).load_weights(str(p))
     assert ei.value.kind == "NoConfig"
+
+
+@pytest.mark.parametrize("precision,tol,S", [("f32", F32_TOL, 40), ("bf16", BF16_TOL, 150)])
+def test_fully_masked_conditions(gpu, pkg, oracle, synth, small_ckpt, precision, tol, S):
+    """A batch in which utterance 0 has every text position masked, utterance
+    1 has every speaker-reference frame masked (no speaker key at all, the
+    masked-mean token masked too: src/model/dit/aux_conditioner.rs:161-190)
+    and utterance 2 is normal; independent CFG over both signals.  The
+    engine's compacted context cache holds no key for the masked parts; the
+    oracle runs the reference's masked attention."""
+    cfg = synth.SMALL_CONFIG
+    r = synth.make_request(cfg, 3, 24, 30, S, seed=21)
+    r["text_mask"][0] = False
+    r["ref_mask"][1] = False
+    W = oracle.Weights.load(str(small_ckpt))
+    req = oracle.SamplingRequest(text_ids=r["text_ids"], text_mask=r["text_mask"], sequence_length=S,
+                                 ref_latent=r["ref_latent"], ref_mask=r["ref_mask"],
+                                 initial_noise=r["initial_noise"])
+    with torch.no_grad():
+        ref = oracle.sample_euler_rf_cfg(W, req, oracle_params(oracle, "euler", "independent", 3)).numpy()
+    eng = (pkg.InferenceBuilder(0).load_weights(str(small_ckpt), precision=precision)
+           .with_sampling(engine_params(pkg, "euler", "independent", 3)).build())
+    out = eng.sample(pkg.SamplingRequest(text_ids=r["text_ids"], text_mask=r["text_mask"], sequence_length=S,
+                                         ref_latent=r["ref_latent"], ref_mask=r["ref_mask"],
+                                         initial_noise=r["initial_noise"]))
+    assert np.isfinite(out).all()
+    for b in range(3):
+        err = rel_l2(out[b], ref[b])
+        assert err < tol, (b, err)
+
+
+@pytest.mark.parametrize("precision,tol", [("f32", F32_TOL), ("bf16", BF16_TOL)])
+def test_single_frame_and_tiny_conditions(gpu, pkg, oracle, synth, small_ckpt, precision, tol):
+    """The smallest request: one latent frame, one text token, one speaker
+    frame (every GEMM below the tensor-core tile, attention over 1 + 1 + 2
+    keys)."""
+    out, ref, _ = run_pair(pkg, oracle, synth, small_ckpt, synth.SMALL_CONFIG, precision, "euler", "independent",
+                           steps=3, B=1, T=1, R=1, S=1)
+    assert np.isfinite(out).all()
+    assert rel_l2(out, ref) < tol, rel_l2(out, ref)
