@@ -329,6 +329,56 @@ def row_case(M, steps):
     return us, nbytes / (us * 1e-6) / 1e9
 
 
+def simt_case(steps, steps_per_request=40):
+    """Profiling case: the f32 SIMT GEMMs that build one request's per-step
+    tables (gemm_simt_kernel, engine.cu cond_module + adaLN), at the default
+    ModelConfig (D = 2048, 24 layers, adaLN rank 256, timestep embedding 512)
+    and steps_per_request + 1 timestep rows: the three cond_module layers,
+    then per adaLN kind (attention, MLP, gate) the down projection of all
+    layers at once and the batched (layer, half) up projections.  `steps`
+    repetitions of the ten launches timed with CUDA events.  Returns (ms per
+    request, TFLOP/s)."""
+    import torch
+    L = ctypes.CDLL(str(PKG_DIR / "libirodori_b200_testhooks.so"))
+    L.irtt_gemm_simt.argtypes = ([ctypes.c_void_p, ctypes.c_int, ctypes.c_long, ctypes.c_long] * 2
+                                 + [ctypes.c_void_p, ctypes.c_long, ctypes.c_long] + [ctypes.c_int] * 4)
+    L.irtt_last_error.restype = ctypes.c_char_p
+    NT, D, NL, R, TE = steps_per_request + 1, 2048, 24, 256, 512
+    g = torch.Generator(device="cuda").manual_seed(0)
+    rnd = lambda *s: torch.randn(*s, device="cuda", generator=g)  # noqa: E731
+    temb, h0, h1, ce = rnd(NT, TE), rnd(NT, D), rnd(NT, D), rnd(NT, 3 * D)
+    cm = [rnd(D, TE) * 0.02, rnd(D, D) * 0.02, rnd(3 * D, D) * 0.02]
+    down = [rnd(NL * 2 * R, D) * 0.02 for _ in range(3)]
+    up = [rnd(NL * 2, D, R) * 0.02 for _ in range(3)]
+    dn = torch.empty(NT, NL * 2 * R, device="cuda")
+    raw = torch.empty(NL * 2, NT, D, device="cuda")
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    calls = [(temb, TE, 0, cm[0], TE, 0, h0, D, 0, D, TE, 1),
+             (h0, D, 0, cm[1], D, 0, h1, D, 0, D, D, 1),
+             (h1, D, 0, cm[2], D, 0, ce, 3 * D, 0, 3 * D, D, 1)]
+    for k in range(3):
+        calls.append((ce[:, k * D:], 3 * D, 0, down[k], D, 0, dn, NL * 2 * R, 0, NL * 2 * R, D, 1))
+        calls.append((dn, NL * 2 * R, R, up[k], R, D * R, raw, D, NT * D, D, R, NL * 2))
+    flops = sum(2.0 * NT * c[9] * c[10] * c[11] for c in calls)
+
+    def request():
+        for a, lda, abs_, b, ldb, bbs, c, ldc, cbs, n, kk, batch in calls:
+            if L.irtt_gemm_simt(P(a), 0, lda, abs_, P(b), 0, ldb, bbs, P(c), ldc, cbs, NT, n, kk, batch):
+                raise RuntimeError(L.irtt_last_error().decode())
+
+    for _ in range(3):
+        request()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        request()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return ms, flops / (ms * 1e-3) / 1e12
+
+
 def attn_case(steps, which="c3"):
     """Profiling case: the joint attention of one DiT layer, H = 16, hd = 128,
     bf16, through the tcgen05 kernel; `steps` launches timed with CUDA events.
@@ -621,6 +671,8 @@ def main():
     ap.add_argument("--ckpt", default=None)
     ap.add_argument("--row-case", type=int, default=0,
                     help="profiling case: the adaLN modulate row kernel alone at M rows, --steps launches")
+    ap.add_argument("--simt-case", action="store_true",
+                    help="profiling case: the f32 SIMT GEMMs of one config-3 request's step tables, --steps times")
     ap.add_argument("--shard", type=int, default=0,
                     help="profiling case: time every rank's config-4 bin of an N-way split on this one GPU")
     ap.add_argument("--latency-only", action="store_true",
@@ -644,6 +696,12 @@ def main():
         peak = measured_peaks()[1]
         print(json.dumps({"row_case_M": args.row_case, "us_per_launch": round(us, 2), "gbs": round(gbs, 1),
                           "hbm_peak_gbs": peak, "frac": round(gbs / peak, 4)}), flush=True)
+        return 0
+    if args.simt_case:
+        load_pkg()
+        ms, tf = simt_case(args.steps)
+        print(json.dumps({"simt_case": "config-3 request step tables (41 rows)", "ms_per_request": round(ms, 4),
+                          "tflops": round(tf, 2)}), flush=True)
         return 0
     if args.codec_only:
         return codec_only(args)

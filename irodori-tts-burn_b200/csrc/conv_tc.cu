@@ -91,11 +91,6 @@ __device__ __forceinline__ int out_row(const ConvTcArgs& a, int phase, int q) {
   return a.convt ? (q + (phase < a.pad ? 1 : 0)) * a.stride + phase - a.pad : q;
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&t);
-}
-
 // Snake with a precomputed 1 / (alpha + 1e-9); the hardware sine (MUFU) is
 // ample for a bf16 output.
 __device__ __forceinline__ float snake_inv(float v, float al, float inv) {

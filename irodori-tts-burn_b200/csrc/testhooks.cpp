@@ -54,6 +54,16 @@ IRTT_API int irtt_gemm_store(const void* A, const void* B, int M, int N, int K, 
   });
 }
 
+// The SIMT GEMM as the engine calls it: batched, strided, f32 or bf16
+// operands, raw f32 output (C[z][m][n] = sum_k A[z][m][k] B[z][n][k]), on the
+// legacy stream without synchronising (callers check with irtt_sync_check()).
+IRTT_API int irtt_gemm_simt(const void* A, int a_bf16, long lda, long a_bs, const void* B, int b_bf16, long ldb,
+                            long b_bs, float* C, long ldc, long c_bs, int M, int N, int K, int batch) {
+  return guard([&] {
+    irt::gemm_simt(A, a_bf16, lda, a_bs, B, b_bf16, ldb, b_bs, C, ldc, c_bs, M, N, K, batch, nullptr);
+  });
+}
+
 // Fused-epilogue GEMM for the QKVG / SWIGLU / RESID modes with bf16 operands.
 IRTT_API int irtt_gemm_epi(int mode, const void* A, const void* B, int M, int N, int K, int path, void* o0, void* o1,
                            void* o2, void* o3, const float* w0, const float* w1, const float* cos_t,

@@ -114,6 +114,48 @@ def test_gemm_qkvg_epilogue(dev, path):
         assert err < 1e-2, f"{name}: rel err {err}"
 
 
+# (M, N, K, batch, bf16 operands, A row pitch, A batch stride): the engine's
+# adaLN-table and cond_module shapes (one row per timestep), tails in every
+# dimension, the scalar-load path (K % 4 != 0, bf16) and the cluster K-split
+# (few tiles) as well as the unsplit batched path.
+SIMT_CASES = [
+    (41, 12288, 2048, 1, 0, 3 * 2048, 0),     # adaLN down, A = silu(c) slice of the 3-D row
+    (41, 2048, 256, 48, 0, 48 * 256, 256),    # adaLN up, batched over (layer, half)
+    (41, 2048, 512, 1, 0, 512, 0),            # cond_module layer 0 (8-way split)
+    (5, 2048, 2048, 1, 0, 2048, 0),           # 4-step request
+    (5, 70, 300, 2, 0, 300, 300 * 5),         # tails, split into 5
+    (5, 70, 301, 2, 0, 301, 301 * 5),         # scalar loads (K % 4 != 0)
+    (65, 130, 1000, 1, 1, 1000, 0),           # bf16 operands, M / N tails
+    (1, 64, 64, 1, 0, 64, 0),                 # single row, single k-tile pair
+]
+
+
+@pytest.mark.parametrize("M,N,K,batch,bf,lda,a_bs", SIMT_CASES)
+def test_gemm_simt_batched_strided(dev, M, N, K, batch, bf, lda, a_bs):
+    L = hooks()
+    L.irtt_gemm_simt.argtypes = ([ctypes.c_void_p, ctypes.c_int, ctypes.c_long, ctypes.c_long] * 2
+                                 + [ctypes.c_void_p, ctypes.c_long, ctypes.c_long] + [ctypes.c_int] * 4)
+    g = torch.Generator(device=dev).manual_seed(M * 7 + N + K)
+    dt = torch.bfloat16 if bf else torch.float32
+    a_store = torch.randn(max(a_bs * (batch - 1) + (M - 1) * lda + K, 1), device=dev, generator=g).to(dt)
+    B = torch.randn(batch, N, K, device=dev, generator=g).to(dt)
+    C = torch.full((batch, M, N + 3), float("nan"), device=dev)
+    A = torch.as_strided(a_store, (batch, M, K), (a_bs, lda, 1))
+    ref = torch.einsum("zmk,znk->zmn", A.double(), B.double())
+    rc = L.irtt_gemm_simt(ptr(a_store), bf, lda, a_bs, ptr(B), bf, K, N * K, ptr(C), N + 3, M * (N + 3), M, N, K,
+                          batch)
+    check(rc)
+    out = C[:, :, :N].double()
+    err = ((out - ref).norm() / ref.norm()).item()
+    assert err < 1e-6, err
+    assert torch.isnan(C[:, :, N:]).all(), "wrote outside the N columns"
+    # the K split sums the partial tiles in a fixed order: bit-identical reruns
+    C2 = torch.full_like(C, float("nan"))
+    check(L.irtt_gemm_simt(ptr(a_store), bf, lda, a_bs, ptr(B), bf, K, N * K, ptr(C2), N + 3, M * (N + 3), M, N, K,
+                           batch))
+    assert torch.equal(C[:, :, :N], C2[:, :, :N])
+
+
 @pytest.mark.parametrize("path", [0, 1])
 def test_gemm_swiglu_and_resid(dev, path):
     M, D, F = 257, 256, 736
