@@ -62,23 +62,39 @@ constexpr uint32_t A_BYTES = BM * BK * 2;
 // measured no faster and cost the 192-wide layers a pipeline stage.)
 constexpr uint32_t EPI_SET = 6144;
 
-template <int BN>
+// Residual stride-1 convolutions (the ResUnits' 1x1, x += conv) use a ring of
+// RES_SETS f32 staging tiles per epilogue warp: each 32 x 32 residual chunk is
+// loaded by TMA into a tile two chunks ahead, the output overwrites it in
+// place and leaves by TMA store from the same tile; one bf16 tile per warp
+// stages the Snake output.  The ring takes 14 KB per warp, so these launches
+// run with the pipeline stages that fit beside it (2-4; their K is 2-12
+// k-blocks and the MMAs are not what bounds them).
+constexpr int RES_SETS = 3;
+constexpr uint32_t RES_SLOT = RES_SETS * 4096 + 2048;
+constexpr uint32_t SMEM_MAX = 232448;  // 227 KB opt-in per CTA
+
+template <int BN, bool RING>
 struct Cfg {
-  static constexpr uint32_t EPI_SLOT = EPI_SET;
+  static constexpr uint32_t EPI_SLOT = RING ? RES_SLOT : EPI_SET;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr uint32_t STAGE_BUDGET = 176 * 1024;
+  // barriers: full / empty per stage, two accumulator pairs, the TMEM slot
+  // (256 B), then the residual ring's (EPI_WARPS x RES_SETS)
+  static constexpr uint32_t BAR_BYTES = RING ? 512 : 256;
+  static constexpr uint32_t STAGE_BUDGET =
+      RING ? SMEM_MAX - 1024 - EPI_WARPS * EPI_SLOT - BAR_BYTES : 176 * 1024;
   static constexpr int STAGES = STAGE_BUDGET / STAGE_BYTES > 8 ? 8 : STAGE_BUDGET / STAGE_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
   // second accumulator at a power-of-two column offset
   static constexpr uint32_t ACC_STRIDE = TMEM_COLS / 2;
-  // alignment slack | stages | epilogue slots (1024-aligned) | barriers (256 B)
+  // alignment slack | stages | epilogue slots (1024-aligned) | barriers
   static constexpr uint32_t OFF_EPI = STAGES * STAGE_BYTES;
   static constexpr uint32_t OFF_BAR = OFF_EPI + EPI_WARPS * EPI_SLOT;
-  static_assert(STAGES >= 3, "at least three pipeline stages");
-  static constexpr size_t SMEM = 1024 + (size_t)OFF_BAR + 256;
+  static_assert(STAGES >= (RING ? 2 : 3), "pipeline stages");
+  static constexpr size_t SMEM = 1024 + (size_t)OFF_BAR + BAR_BYTES;
+  static_assert(SMEM <= SMEM_MAX, "shared memory");
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN);
-  static_assert((OFF_EPI % 1024) == 0, "epilogue slots must be 1024-byte aligned");
+  static_assert((OFF_EPI % 1024) == 0 && (EPI_SLOT % 1024) == 0, "epilogue tiles must be 1024-byte aligned");
   static_assert(32 * 33 * 4 <= EPI_SET, "transpose buffer fits a slot");
 };
 
@@ -98,18 +114,19 @@ __device__ __forceinline__ float snake_inv(float v, float al, float inv) {
   return v + s * s * inv;
 }
 
-template <int BN>
+template <int BN, bool RING>
 __global__ void __launch_bounds__(THREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmP,
                    const __grid_constant__ ConvTcArgs a) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, RING>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  uint64_t* rbars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR + 256);  // RING: [warp][set]
   uint8_t* epi = smem + C::OFF_EPI;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -140,6 +157,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(tfull(b), 1);
       mbar_init(tempty(b), EPI_WARPS);
     }
+    if constexpr (RING)
+      for (int i = 0; i < EPI_WARPS * RES_SETS; ++i) mbar_init(smem_u32(&rbars[i]), 1);
     mbar_fence_init();
     prefetch_map(&tmA);
     prefetch_map(&tmB);
@@ -209,7 +228,109 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int quad = warp & 3;              // TMEM lane quadrant this warp may access
     const int half = (warp - 2) / 4;        // which 32-column chunks it takes
     uint8_t* slot = epi + (warp - 2) * C::EPI_SLOT;
-    if (!a.convt) {
+    if constexpr (RING) {
+      // Residual 1x1 convolutions (the launcher takes RING only for stride-1,
+      // x += conv): thread = output row as below, the residual chunk read from
+      // this warp's ring tile (see Cfg).  The warp's chunks are numbered
+      // g = 0, 1, ...: unit i = g / npu of this CTA, column 32 * half + 64 * (g % npu).
+      const int npu = BN > 32 * half ? (BN - 32 * half + 63) / 64 : 0;
+      const int my_units = (int)blockIdx.x < units ? (units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+      const int nchunks = npu * my_units;
+      uint64_t* rb = rbars + (warp - 2) * RES_SETS;
+      uint8_t* ps = slot + RES_SETS * 4096;  // bf16 [32][32], 64-byte swizzle
+      // lane 0: residual chunk g (32 rows x 32 f32, 128-byte swizzle) into its ring tile
+      auto res_load = [&](int g) {
+        const int i = g / npu;
+        int mi, ph, ni;
+        unit_coords((int)blockIdx.x + i * (int)gridDim.x, mi, ph, ni);
+        const int set = g % RES_SETS;
+        const uint32_t bar = smem_u32(&rb[set]);
+        mbar_expect_tx(bar, 4096);
+        tma_load_2d(smem_u32(slot + set * 4096), &tmX, bar, ni * BN + 32 * half + 64 * (g - i * npu),
+                    mi * BM + quad * 32);
+      };
+      if (lane == 0)
+        for (int g = 0; g < RES_SETS - 1 && g < nchunks; ++g) res_load(g);
+      int g = 0;
+      uint32_t tl = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x, ++tl) {
+        int mi, ph, ni;
+        unit_coords(u, mi, ph, ni);
+        const int m0 = mi * BM, n0 = ni * BN;
+        const int buf = tl & 1;
+        const int q0 = m0 + quad * 32;
+        const int row = q0 + lane;
+        const bool valid = row < a.rows_in && a.frame_src[row / a.out_scale] >= 0;
+        mbar_wait(tfull(buf), (tl >> 1) & 1);
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * C::ACC_STRIDE;
+#pragma unroll 1
+        for (int c = 32 * half; c < BN; c += 64, ++g) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c, r);
+          // the previous chunk's stores have read their tiles, so its ring
+          // tile takes the residual chunk two ahead
+          if (lane == 0) {
+            bulk_wait_read0();
+            if (g + RES_SETS - 1 < nchunks) res_load(g + RES_SETS - 1);
+          }
+          __syncwarp();
+          tmem_wait_ld();
+          const int set = g % RES_SETS;
+          mbar_wait(smem_u32(&rb[set]), (uint32_t)(g / RES_SETS) & 1);
+          uint8_t* xs = slot + set * 4096;  // residual in, f32 output out (same layout)
+          const float* bp = a.bias ? a.bias + n0 + c : nullptr;
+          const float* ap = a.alpha ? a.alpha + n0 + c : nullptr;
+          const float* ip = a.alpha ? a.alpha_inv + n0 + c : nullptr;
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {  // 8 columns: one 16-byte chunk of the bf16 row
+            float v[8];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int k = 2 * m + h;  // float4 group: columns 4k .. 4k + 3
+              float4* xp = reinterpret_cast<float4*>(xs + lane * 128 + ((k ^ (lane & 7)) << 4));
+              const float4 xr = *xp;
+              const float4 b4 = bp ? reinterpret_cast<const float4*>(bp)[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+              float w0 = __uint_as_float(r[4 * k]) + b4.x + xr.x, w1 = __uint_as_float(r[4 * k + 1]) + b4.y + xr.y;
+              float w2 = __uint_as_float(r[4 * k + 2]) + b4.z + xr.z, w3 = __uint_as_float(r[4 * k + 3]) + b4.w + xr.w;
+              if (!valid) w0 = w1 = w2 = w3 = 0.f;
+              *xp = make_float4(w0, w1, w2, w3);
+              if (ap) {
+                const float4 al = reinterpret_cast<const float4*>(ap)[k];
+                const float4 in = reinterpret_cast<const float4*>(ip)[k];
+                w0 = snake_inv(w0, al.x, in.x);
+                w1 = snake_inv(w1, al.y, in.y);
+                w2 = snake_inv(w2, al.z, in.z);
+                w3 = snake_inv(w3, al.w, in.w);
+              }
+              v[4 * h] = w0;
+              v[4 * h + 1] = w1;
+              v[4 * h + 2] = w2;
+              v[4 * h + 3] = w3;
+            }
+            if (a.p) {
+              uint4 pk;
+              pk.x = pack_bf16x2(v[0], v[1]);
+              pk.y = pack_bf16x2(v[2], v[3]);
+              pk.z = pack_bf16x2(v[4], v[5]);
+              pk.w = pack_bf16x2(v[6], v[7]);
+              *reinterpret_cast<uint4*>(ps + lane * 64 + ((m ^ ((lane >> 1) & 3)) << 4)) = pk;
+            }
+          }
+          fence_proxy_async();  // generic-proxy smem writes -> visible to the TMA stores
+          __syncwarp();
+          if (lane == 0 && q0 < a.rows_out) {  // rows past the end are clipped by the TMA unit
+            tma_store_2d(&tmX, smem_u32(xs), n0 + c, q0);
+            if (a.p) tma_store_2d(&tmP, smem_u32(ps), n0 + c, q0);
+            bulk_commit();
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty(buf));
+      }
+      if (lane == 0) bulk_wait0();  // every store of this warp has completed
+    } else if (!a.convt) {
       // Stride-1 convolutions (output row = GEMM row): thread = output row.
       // Each 32 x 32 chunk leaves through this warp's staging tiles by TMA
       // stores (f32 residual stream, bf16 Snake output); the residual rows
@@ -482,9 +603,9 @@ int num_sms() {
   return n;
 }
 
-template <int BN>
+template <int BN, bool RING>
 void launch(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, RING>;
   static unsigned attr_mask = 0;  // per-device opt-in to the large dynamic smem
   static std::mutex mu;
   int dev = 0;
@@ -492,7 +613,8 @@ void launch(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) 
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!(attr_mask & (1u << (dev & 31)))) {
-      IRT_CUDA(cudaFuncSetAttribute(conv_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
+      IRT_CUDA(cudaFuncSetAttribute(conv_tc_kernel<BN, RING>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)C::SMEM));
       attr_mask |= 1u << (dev & 31);
     }
   }
@@ -506,8 +628,15 @@ void launch(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) 
   // (any valid map) for ConvTranspose
   const CUtensorMap tx = (!a.convt && a.x) ? tma_map_tile32(a.x, true, a.rows_out, a.cout, a.cout) : ta;
   const CUtensorMap tp = (!a.convt && a.p) ? tma_map_tile32(a.p, false, a.rows_out, a.cout, a.cout) : ta;
-  launch_pdl(conv_tc_kernel<BN>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, tx, tp, a);
+  launch_pdl(conv_tc_kernel<BN, RING>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, tx, tp, a);
   IRT_CHECK_LAUNCH();
+}
+
+// Residual stride-1 convolutions take the residual ring (see Cfg).
+template <int BN>
+void launch(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) {
+  if (!a.convt && a.add_res && a.x) launch<BN, true>(in, w, a, s);
+  else launch<BN, false>(in, w, a, s);
 }
 
 }  // namespace ctc
