@@ -73,24 +73,41 @@ constexpr int RES_SETS = 3;
 constexpr uint32_t RES_SLOT = RES_SETS * 4096 + 2048;
 constexpr uint32_t SMEM_MAX = 232448;  // 227 KB opt-in per CTA
 
-template <int BN, bool RING>
+// Stride-1 convolutions with k > 1 (the ResUnits' dilated k7, the stem) stage
+// the input rows of a unit ONCE per 64-channel block: one TMA box of
+// 128 + (k - 1) * dilation rows (the unit's rows with the halo every tap
+// needs) in a two-slot ring, and tap t's MMAs read it through a descriptor
+// that starts t * dilation rows in (the 128-byte swizzle is a function of the
+// shared-memory address, and the box is written 1024-byte aligned, so a
+// row-shifted view reads the rows it names).  The pipeline stages then carry
+// only the weight tiles: one input load per channel block instead of one per
+// tap.
+constexpr int HALO_ROWS_MAX = 184;
+constexpr uint32_t HALO_SLOT = HALO_ROWS_MAX * 128;
+
+// VAR: 0 plain, 1 residual ring (1x1, x += conv), 2 halo (stride 1, k > 1)
+template <int BN, int VAR>
 struct Cfg {
-  static constexpr uint32_t EPI_SLOT = RING ? RES_SLOT : EPI_SET;
+  static constexpr uint32_t EPI_SLOT = VAR == 1 ? RES_SLOT : EPI_SET;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
-  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  // barriers: full / empty per stage, two accumulator pairs, the TMEM slot
-  // (256 B), then the residual ring's (EPI_WARPS x RES_SETS)
-  static constexpr uint32_t BAR_BYTES = RING ? 512 : 256;
+  static constexpr uint32_t STAGE_BYTES = VAR == 2 ? B_BYTES : A_BYTES + B_BYTES;
+  static constexpr uint32_t HALO_BYTES = VAR == 2 ? 2 * HALO_SLOT : 0;
+  // barriers: full / empty per stage, two accumulator pairs, the TMEM slot,
+  // the halo ring's (256 B), then the residual ring's (EPI_WARPS x RES_SETS)
+  static constexpr uint32_t BAR_BYTES = VAR == 1 ? 512 : 256;
   static constexpr uint32_t STAGE_BUDGET =
-      RING ? SMEM_MAX - 1024 - EPI_WARPS * EPI_SLOT - BAR_BYTES : 176 * 1024;
+      VAR == 0 ? 176 * 1024 : SMEM_MAX - 1024 - EPI_WARPS * EPI_SLOT - HALO_BYTES - BAR_BYTES;
   static constexpr int STAGES = STAGE_BUDGET / STAGE_BYTES > 8 ? 8 : STAGE_BUDGET / STAGE_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
   // second accumulator at a power-of-two column offset
   static constexpr uint32_t ACC_STRIDE = TMEM_COLS / 2;
-  // alignment slack | stages | epilogue slots (1024-aligned) | barriers
-  static constexpr uint32_t OFF_EPI = STAGES * STAGE_BYTES;
+  // alignment slack | stages | halo slots | epilogue slots (1024-aligned) | barriers
+  static constexpr uint32_t OFF_HALO = STAGES * STAGE_BYTES;
+  static constexpr uint32_t OFF_EPI = OFF_HALO + HALO_BYTES;
   static constexpr uint32_t OFF_BAR = OFF_EPI + EPI_WARPS * EPI_SLOT;
-  static_assert(STAGES >= (RING ? 2 : 3), "pipeline stages");
+  static_assert(STAGES >= (VAR == 0 ? 3 : 2), "pipeline stages");
+  static_assert(VAR != 2 || (OFF_HALO % 1024) == 0, "halo slots must be 1024-byte aligned");
+  static_assert(2 * STAGES + 5 + 4 <= 32, "barrier region");
   static constexpr size_t SMEM = 1024 + (size_t)OFF_BAR + BAR_BYTES;
   static_assert(SMEM <= SMEM_MAX, "shared memory");
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN);
@@ -114,12 +131,13 @@ __device__ __forceinline__ float snake_inv(float v, float al, float inv) {
   return v + s * s * inv;
 }
 
-template <int BN, bool RING>
+template <int BN, int VAR>
 __global__ void __launch_bounds__(THREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmP,
                    const __grid_constant__ ConvTcArgs a) {
-  using C = Cfg<BN, RING>;
+  using C = Cfg<BN, VAR>;
+  constexpr bool RING = VAR == 1, HALO = VAR == 2;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -127,6 +145,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   uint64_t* rbars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR + 256);  // RING: [warp][set]
+  uint64_t* hbars = bars + 2 * STAGES + 5;  // HALO: full[2], empty[2]
   uint8_t* epi = smem + C::OFF_EPI;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -159,6 +178,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if constexpr (RING)
       for (int i = 0; i < EPI_WARPS * RES_SETS; ++i) mbar_init(smem_u32(&rbars[i]), 1);
+    if constexpr (HALO)
+      for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&hbars[i]), 1);
     mbar_fence_init();
     prefetch_map(&tmA);
     prefetch_map(&tmB);
@@ -172,7 +193,69 @@ __global__ void __launch_bounds__(THREADS, 1)
   pdl_wait();
   pdl_trigger();
 
-  if (warp == 0) {
+  // HALO: rows of one staged input block (the unit's 128 plus every tap's shift)
+  const int halo_rows = BM + (a.taps - 1) * a.dil;
+  auto hfull = [&](int i) { return smem_u32(&hbars[i]); };
+  auto hempty = [&](int i) { return smem_u32(&hbars[2 + i]); };
+  uint8_t* halo = smem + C::OFF_HALO;
+
+  if (HALO && warp == 0) {
+    // ---------------- TMA producer (halo staging) ----------------
+    if (lane == 0) {
+      uint32_t it = 0, hit = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        int mi, ph, ni;
+        unit_coords(u, mi, ph, ni);
+        const int m0 = mi * BM, n0 = ni * BN;
+        for (int cb = 0; cb < kpt; ++cb, ++hit) {
+          const int hs = hit & 1;
+          mbar_wait(hempty(hs), ((hit >> 1) & 1) ^ 1);
+          mbar_expect_tx(hfull(hs), (uint32_t)halo_rows * 128);
+          tma_load_2d(smem_u32(halo + hs * HALO_SLOT), &tmA, hfull(hs), cb * BK, m0 - a.pad);
+          for (int tap = 0; tap < a.taps; ++tap, ++it) {
+            const int s = it % STAGES;
+            mbar_wait(empty(s), ((it / STAGES) & 1) ^ 1);
+            mbar_expect_tx(full(s), C::STAGE_BYTES);
+            tma_load_2d(smem_u32(tiles + s * C::STAGE_BYTES), &tmB, full(s), tap * a.cin_pad + cb * BK, n0);
+          }
+        }
+      }
+    }
+  } else if (HALO && warp == 1) {
+    // ---------------- MMA issuer (halo staging) ----------------
+    if (lane == 0) {
+      uint32_t it = 0, hit = 0, tl = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x, ++tl) {
+        const int buf = tl & 1;
+        mbar_wait(tempty(buf), ((tl >> 1) & 1) ^ 1);
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * C::ACC_STRIDE;
+        for (int cb = 0; cb < kpt; ++cb, ++hit) {
+          const int hs = hit & 1;
+          // input channels past cin are zero padding: skip their MMAs
+          const int nkk = min(BK / 16, (a.cin - cb * BK + 15) / 16);
+          mbar_wait(hfull(hs), (hit >> 1) & 1);
+          tc_fence_after();
+          const uint32_t h_addr = smem_u32(halo + hs * HALO_SLOT);
+          for (int tap = 0; tap < a.taps; ++tap, ++it) {
+            const int s = it % STAGES;
+            mbar_wait(full(s), (it / STAGES) & 1);
+            tc_fence_after();
+            const uint32_t a_addr = h_addr + (uint32_t)(tap * a.dil) * 128u;  // rows shifted by the tap
+            const uint32_t b_addr = smem_u32(tiles + s * C::STAGE_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              if (kk < nkk)
+                umma_f16(d_tmem, sdesc_kmajor(a_addr + kk * 32), sdesc_kmajor(b_addr + kk * 32), C::IDESC,
+                         (cb | tap | kk) ? 1u : 0u);
+            umma_commit(empty(s));  // frees the weight stage when these MMAs complete
+          }
+          umma_commit(hempty(hs));  // frees the staged input block
+        }
+        umma_commit(tfull(buf));  // accumulator ready
+      }
+    }
+  } else if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       uint32_t it = 0;
@@ -603,9 +686,9 @@ int num_sms() {
   return n;
 }
 
-template <int BN, bool RING>
+template <int BN, int VAR>
 void launch(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) {
-  using C = Cfg<BN, RING>;
+  using C = Cfg<BN, VAR>;
   static unsigned attr_mask = 0;  // per-device opt-in to the large dynamic smem
   static std::mutex mu;
   int dev = 0;
@@ -613,13 +696,14 @@ void launch(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) 
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!(attr_mask & (1u << (dev & 31)))) {
-      IRT_CUDA(cudaFuncSetAttribute(conv_tc_kernel<BN, RING>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      IRT_CUDA(cudaFuncSetAttribute(conv_tc_kernel<BN, VAR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)C::SMEM));
       attr_mask |= 1u << (dev & 31);
     }
   }
   // copies: the map cache may be cleared by another thread
-  const CUtensorMap ta = tma_map_bf16(in, a.rows_in, a.cin, a.cin, BM);
+  // HALO: one box spans the unit's rows plus every tap's shift
+  const CUtensorMap ta = tma_map_bf16(in, a.rows_in, a.cin, a.cin, VAR == 2 ? BM + (a.taps - 1) * a.dil : BM);
   const long kcols = (long)a.taps * a.cin_pad;
   const CUtensorMap tb = tma_map_bf16(w, (long)a.phases * a.cout, kcols, kcols, BN);
   const long units = (long)((a.rows_in + BM - 1) / BM) * a.phases * (a.cout / BN);
@@ -628,15 +712,17 @@ void launch(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) 
   // (any valid map) for ConvTranspose
   const CUtensorMap tx = (!a.convt && a.x) ? tma_map_tile32(a.x, true, a.rows_out, a.cout, a.cout) : ta;
   const CUtensorMap tp = (!a.convt && a.p) ? tma_map_tile32(a.p, false, a.rows_out, a.cout, a.cout) : ta;
-  launch_pdl(conv_tc_kernel<BN, RING>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, tx, tp, a);
+  launch_pdl(conv_tc_kernel<BN, VAR>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, tx, tp, a);
   IRT_CHECK_LAUNCH();
 }
 
-// Residual stride-1 convolutions take the residual ring (see Cfg).
+// Residual stride-1 convolutions take the residual ring, other stride-1
+// convolutions with k > 1 the halo staging (see Cfg).
 template <int BN>
 void launch(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) {
-  if (!a.convt && a.add_res && a.x) launch<BN, true>(in, w, a, s);
-  else launch<BN, false>(in, w, a, s);
+  if (!a.convt && a.add_res && a.x) launch<BN, 1>(in, w, a, s);
+  else if (!a.convt && a.taps > 1 && BM + (a.taps - 1) * a.dil <= HALO_ROWS_MAX) launch<BN, 2>(in, w, a, s);
+  else launch<BN, 0>(in, w, a, s);
 }
 
 }  // namespace ctc
