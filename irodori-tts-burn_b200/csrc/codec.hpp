@@ -27,6 +27,7 @@ struct ConvTcArgs {
   float* x = nullptr;              // f32 output rows [rows_out, cout] (nullptr: not written)
   int add_res = 0;                 // x = x + conv (residual, in place)
   bf16* p = nullptr;               // bf16 output rows [rows_out, cout] (nullptr: not written)
+  int ct_tma = 0;                  // ConvTranspose outputs by phased TMA stores (set by conv_tc)
 };
 
 int conv_tc_bn(int cout);

@@ -44,6 +44,8 @@ namespace irt {
 const CUtensorMap& tma_map_bf16(const void* p, long rows, long cols, long ld, int box_rows);
 // {32, 32} boxes: f32 with the 128-byte swizzle or bf16 with the 64-byte swizzle (gemm_tc.cu).
 CUtensorMap tma_map_tile32(const void* p, bool f32, long rows, long cols, long ld);
+// the same tiles over the rows q * s + r of one phase r, as (column, r, q) (gemm_tc.cu).
+CUtensorMap tma_map_tile32_phased(const void* p, bool f32, long q_rows, long cols, int s);
 
 namespace ctc {
 
@@ -413,8 +415,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) mbar_arrive(tempty(buf));
       }
       if (lane == 0) bulk_wait0();  // every store of this warp has completed
-    } else if (!a.convt) {
-      // Stride-1 convolutions (output row = GEMM row): thread = output row.
+    } else if (!a.convt || a.ct_tma) {
+      // Stride-1 convolutions (output row = GEMM row), and ConvTranspose
+      // phases whose output rows o = q * stride + r leave by 3-D TMA stores
+      // (column, r, q): thread = GEMM row.
       // Each 32 x 32 chunk leaves through this warp's staging tiles by TMA
       // stores (f32 residual stream, bf16 Snake output); the residual rows
       // are read straight into registers (a float4 per 4 columns) one chunk
@@ -443,7 +447,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int q0 = m0 + quad * 32;
         const int row = q0 + lane;
         const bool ok = row < a.rows_in;
-        const bool valid = ok && a.frame_src[row / a.out_scale] >= 0;
+        // ConvTranspose: output row of GEMM row q in this phase is q * stride + rph
+        const int rph = a.convt ? (ph < a.pad ? a.stride : 0) + ph - a.pad : 0;
+        const int orow = a.convt ? row * a.stride + rph : row;
+        const bool valid = ok && a.frame_src[orow / a.out_scale] >= 0;
+        const int qlim = a.convt ? a.rows_in : a.rows_out;
         mbar_wait(tfull(buf), (tl >> 1) & 1);
         tc_fence_after();
         const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * C::ACC_STRIDE;
@@ -508,9 +516,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           fence_proxy_async();  // generic-proxy smem writes -> visible to the TMA stores
           __syncwarp();
-          if (lane == 0 && q0 < a.rows_out) {  // rows past the end are clipped by the TMA unit
-            if (a.x) tma_store_2d(&tmX, smem_u32(xs), n0 + c, q0);
-            if (a.p) tma_store_2d(&tmP, smem_u32(ps), n0 + c, q0);
+          if (lane == 0 && q0 < qlim) {  // rows past the end are clipped by the TMA unit
+            if (a.convt) {
+              if (a.x) tma_store_3d(&tmX, smem_u32(xs), n0 + c, rph, q0);
+              if (a.p) tma_store_3d(&tmP, smem_u32(ps), n0 + c, rph, q0);
+            } else {
+              if (a.x) tma_store_2d(&tmX, smem_u32(xs), n0 + c, q0);
+              if (a.p) tma_store_2d(&tmP, smem_u32(ps), n0 + c, q0);
+            }
             bulk_commit();
           }
           if (more) {
@@ -710,8 +723,14 @@ void launch(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) 
   const int grid = (int)std::min<long>(units, num_sms());
   // stride-1 path: TMA maps of the outputs (32 x 32 staging tiles); unused
   // (any valid map) for ConvTranspose
-  const CUtensorMap tx = (!a.convt && a.x) ? tma_map_tile32(a.x, true, a.rows_out, a.cout, a.cout) : ta;
-  const CUtensorMap tp = (!a.convt && a.p) ? tma_map_tile32(a.p, false, a.rows_out, a.cout, a.cout) : ta;
+  CUtensorMap tx = ta, tp = ta;
+  if (!a.convt) {
+    if (a.x) tx = tma_map_tile32(a.x, true, a.rows_out, a.cout, a.cout);
+    if (a.p) tp = tma_map_tile32(a.p, false, a.rows_out, a.cout, a.cout);
+  } else if (a.ct_tma) {
+    if (a.x) tx = tma_map_tile32_phased(a.x, true, a.rows_in, a.cout, a.stride);
+    if (a.p) tp = tma_map_tile32_phased(a.p, false, a.rows_in, a.cout, a.stride);
+  }
   launch_pdl(conv_tc_kernel<BN, VAR>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, tx, tp, a);
   IRT_CHECK_LAUNCH();
 }
@@ -745,13 +764,17 @@ void conv_tc(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s)
     throw unsupported("conv_tc: outputs, bias and alpha must be 16-byte aligned");
   if ((long)a.rows_out * a.cout >= (1L << 31) || (long)a.rows_in * a.phases >= (1L << 31))
     throw unsupported("conv_tc: level too large for 32-bit row indices");
+  // ConvTranspose outputs leave by phased TMA stores when every phase has the
+  // same number of rows (rows_out = rows_in * stride; the even strides)
+  ConvTcArgs b = a;
+  b.ct_tma = a.convt && !a.add_res && (long)a.rows_out == (long)a.rows_in * a.stride;
   switch (conv_tc_bn(a.cout)) {
-    case 256: ctc::launch<256>(in, w, a, s); break;
-    case 192: ctc::launch<192>(in, w, a, s); break;
-    case 128: ctc::launch<128>(in, w, a, s); break;
-    case 96: ctc::launch<96>(in, w, a, s); break;
-    case 64: ctc::launch<64>(in, w, a, s); break;
-    case 32: ctc::launch<32>(in, w, a, s); break;
+    case 256: ctc::launch<256>(in, w, b, s); break;
+    case 192: ctc::launch<192>(in, w, b, s); break;
+    case 128: ctc::launch<128>(in, w, b, s); break;
+    case 96: ctc::launch<96>(in, w, b, s); break;
+    case 64: ctc::launch<64>(in, w, b, s); break;
+    case 32: ctc::launch<32>(in, w, b, s); break;
     default: throw unsupported("conv_tc: output channels must be a multiple of 32");
   }
 }

@@ -683,6 +683,25 @@ CUtensorMap tma_map_tile32(const void* p, bool f32, long rows, long cols, long l
   return m;
 }
 
+// The rows o = q * s + r of a [q_rows * s, cols] f32 / bf16 matrix seen as 3-D
+// (column, r, q): {32, 1, 32} boxes select 32 rows of one phase r that are s
+// rows apart (a ConvTranspose output phase), swizzled as tma_map_tile32.
+CUtensorMap tma_map_tile32_phased(const void* p, bool f32, long q_rows, long cols, int s) {
+  CUtensorMap m;
+  const cuuint64_t esz = f32 ? 4 : 2;
+  cuuint64_t gdim[3] = {(cuuint64_t)cols, (cuuint64_t)s, (cuuint64_t)q_rows};
+  cuuint64_t gstride[2] = {(cuuint64_t)cols * esz, (cuuint64_t)s * cols * esz};
+  cuuint32_t box[3] = {32, 1, 32};
+  cuuint32_t estride[3] = {1, 1, 1};
+  CUresult r = tc::get_encode()(&m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                                const_cast<void*>(p), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw Error(IRT_E_CUDA, "cuTensorMapEncodeTiled (phased tile32) failed (" + std::to_string((int)r) + ")");
+  return m;
+}
+
 // bf16 2-D tensor map with a {64, box_rows} box and 128-byte swizzle (cached).
 const CUtensorMap& tma_map_bf16(const void* p, long rows, long cols, long ld, int box_rows) {
   return tc::tensor_map(p, rows, cols, ld, box_rows);

@@ -89,6 +89,7 @@ CASES = [
     ("res_1x1_resid_c384", 30, 10, 384, 384, 1, 1, 0, 1, 1, True),
     ("res_1x1_resid_c96", 40, 8, 96, 96, 1, 1, 0, 1, 1, True),
     ("convt_s2", 300, 1, 192, 96, 4, 1, 1, 2, 0, True),
+    ("convt_s3_odd", 200, 1, 192, 96, 6, 1, 1, 3, 0, True),  # odd stride: phase -> row map
     ("convt_s8", 200, 1, 384, 192, 16, 1, 1, 8, 0, True),
     ("convt_s10", 150, 1, 768, 384, 20, 1, 1, 10, 0, True),
     ("convt_s12", 131, 1, 1536, 768, 24, 1, 1, 12, 0, True),
