@@ -33,6 +33,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "codec.hpp"
@@ -621,6 +622,210 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Narrow dilated convolutions as the transposed product (the ResUnits' k7 at
+// <= 128 output channels, whose M = 128 x N = cout MMAs are too narrow to keep
+// the tensor pipe busy):
+//   D[co, t] = sum_(tap, ci) W[co, tap, ci] * X[t + tap * dil - pad, ci]
+// M = output channels (cout <= 128, rows past cout are don't-care), N = 256
+// time rows per unit, K = (channel block, tap).  A = the weight tile
+// [cout rows x 64 channels] of one (tap, block) on the stage ring; B = the
+// unit's input rows plus every tap's shift, staged once per 64-channel block
+// as two 160-row TMA boxes, tap t read through a descriptor t * dil rows in
+// (as the halo path above).  The accumulator is 128 lanes (channels) x 256
+// columns (time), double-buffered: all 512 TMEM columns.  Epilogue: lane =
+// channel; per 32-row chunk it writes a [time][channel] bf16 tile (one row
+// per store instruction, conflict-free) of Snake(acc + bias), zero on gap
+// rows, and stores it by TMA.  Writes the bf16 output only (the k7 layers
+// feed the 1x1 convolution; they have no residual or f32 stream).
+// ---------------------------------------------------------------------------
+constexpr int NT = 256;            // time rows per unit (the MMA's N)
+constexpr int HBOX = 160;          // rows per input TMA box; two boxes per block
+constexpr int T_HALO_MAX = 2 * HBOX - NT;  // largest (k - 1) * dil
+constexpr uint32_t T_HSLOT = 2 * HBOX * 128;
+constexpr uint32_t T_A_BYTES = 128 * BK * 2;  // weight stage (rows past cout unused)
+constexpr uint32_t T_EPI_SLOT = 2 * 2048;     // two bf16 32 x 32 tiles per warp
+constexpr int T_STAGES =
+    (int)((SMEM_MAX - 1024 - 2 * T_HSLOT - EPI_WARPS * T_EPI_SLOT - 256) / T_A_BYTES) > 8
+        ? 8
+        : (int)((SMEM_MAX - 1024 - 2 * T_HSLOT - EPI_WARPS * T_EPI_SLOT - 256) / T_A_BYTES);
+constexpr uint32_t T_OFF_HALO = T_STAGES * T_A_BYTES;
+constexpr uint32_t T_OFF_EPI = T_OFF_HALO + 2 * T_HSLOT;
+constexpr uint32_t T_OFF_BAR = T_OFF_EPI + EPI_WARPS * T_EPI_SLOT;
+constexpr size_t T_SMEM = 1024 + (size_t)T_OFF_BAR + 256;
+static_assert(T_SMEM <= SMEM_MAX && T_STAGES >= 3, "transposed conv shared memory");
+static_assert((T_OFF_HALO % 1024) == 0 && (T_OFF_EPI % 1024) == 0 && (T_HSLOT % 1024) == 0, "alignment");
+constexpr uint32_t T_IDESC = idesc_bf16(128, NT);
+
+__global__ void __launch_bounds__(THREADS, 1)
+    conv_t_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ CUtensorMap tmW,
+                  const __grid_constant__ CUtensorMap tmP, const __grid_constant__ ConvTcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + T_OFF_BAR);
+  // full[T_STAGES], empty[T_STAGES], hfull[2], hempty[2], tfull[2], tempty[2]; tmem slot
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * T_STAGES + 8);
+  auto full = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty = [&](int s) { return smem_u32(&bars[T_STAGES + s]); };
+  auto hfull = [&](int i) { return smem_u32(&bars[2 * T_STAGES + i]); };
+  auto hempty = [&](int i) { return smem_u32(&bars[2 * T_STAGES + 2 + i]); };
+  auto tfull = [&](int b) { return smem_u32(&bars[2 * T_STAGES + 4 + b]); };
+  auto tempty = [&](int b) { return smem_u32(&bars[2 * T_STAGES + 6 + b]); };
+  uint8_t* halo = smem + T_OFF_HALO;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int units = (a.rows_in + NT - 1) / NT;
+  const int kpt = a.cin_pad / BK;
+  const uint32_t w_bytes = (uint32_t)a.cout * 128;  // weight box: cout rows x 64 channels
+
+  // weight-stage rows past cout are never loaded: zero them once so the
+  // accumulator lanes they feed (never stored) hold finite values
+  for (uint32_t i = threadIdx.x * 16; i < (uint32_t)T_STAGES * T_A_BYTES; i += THREADS * 16)
+    if ((i % T_A_BYTES) >= w_bytes) *reinterpret_cast<uint4*>(smem + i) = make_uint4(0u, 0u, 0u, 0u);
+  fence_proxy_async();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < T_STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(hfull(b), 1);
+      mbar_init(hempty(b), 1);
+      mbar_init(tfull(b), 1);
+      mbar_init(tempty(b), EPI_WARPS);
+    }
+    mbar_fence_init();
+    prefetch_map(&tmIn);
+    prefetch_map(&tmW);
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
+  pdl_trigger();
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t it = 0, hit = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        const int t0 = u * NT;
+        for (int cb = 0; cb < kpt; ++cb, ++hit) {
+          const int hs = hit & 1;
+          mbar_wait(hempty(hs), ((hit >> 1) & 1) ^ 1);
+          mbar_expect_tx(hfull(hs), T_HSLOT);
+          uint8_t* hb = halo + hs * T_HSLOT;
+          tma_load_2d(smem_u32(hb), &tmIn, hfull(hs), cb * BK, t0 - a.pad);
+          tma_load_2d(smem_u32(hb + HBOX * 128), &tmIn, hfull(hs), cb * BK, t0 - a.pad + HBOX);
+          for (int tap = 0; tap < a.taps; ++tap, ++it) {
+            const int s = it % T_STAGES;
+            mbar_wait(empty(s), ((it / T_STAGES) & 1) ^ 1);
+            mbar_expect_tx(full(s), w_bytes);
+            tma_load_2d(smem_u32(smem + s * T_A_BYTES), &tmW, full(s), tap * a.cin_pad + cb * BK, 0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t it = 0, hit = 0, tl = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x, ++tl) {
+        const int buf = tl & 1;
+        mbar_wait(tempty(buf), ((tl >> 1) & 1) ^ 1);
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * NT;
+        for (int cb = 0; cb < kpt; ++cb, ++hit) {
+          const int hs = hit & 1;
+          const int nkk = min(BK / 16, (a.cin - cb * BK + 15) / 16);  // skip zero-padded channels
+          mbar_wait(hfull(hs), (hit >> 1) & 1);
+          tc_fence_after();
+          const uint32_t h_addr = smem_u32(halo + hs * T_HSLOT);
+          for (int tap = 0; tap < a.taps; ++tap, ++it) {
+            const int s = it % T_STAGES;
+            mbar_wait(full(s), (it / T_STAGES) & 1);
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(smem + s * T_A_BYTES);
+            const uint32_t b_addr = h_addr + (uint32_t)(tap * a.dil) * 128u;
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              if (kk < nkk)
+                umma_f16(d_tmem, sdesc_kmajor(a_addr + kk * 32), sdesc_kmajor(b_addr + kk * 32), T_IDESC,
+                         (cb | tap | kk) ? 1u : 0u);
+            umma_commit(empty(s));
+          }
+          umma_commit(hempty(hs));
+        }
+        umma_commit(tfull(buf));
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2 .. 2 + EPI_WARPS ----------------
+    const int quad = warp & 3;        // TMEM lanes = output channels 32 * quad ..
+    const int half = (warp - 2) / 4;  // time columns 128 * half .. + 127
+    const int co = 32 * quad + lane;
+    const bool q_on = 32 * quad < a.cout;  // quads past cout are padding (uniform per warp)
+    const bool c_ok = co < a.cout;
+    const float bv = (c_ok && a.bias) ? a.bias[co] : 0.f;
+    const float al = (c_ok && a.alpha) ? a.alpha[co] : 0.f;
+    const float ai = (c_ok && a.alpha) ? a.alpha_inv[co] : 0.f;
+    uint8_t* st = smem + T_OFF_EPI + (warp - 2) * T_EPI_SLOT;
+    uint32_t tl = 0, g = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++tl) {
+      const int buf = tl & 1;
+      const int t0 = u * NT;
+      mbar_wait(tfull(buf), (tl >> 1) & 1);
+      tc_fence_after();
+      if (q_on) {
+        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * NT;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c, ++g) {
+          const int col = 128 * half + 32 * c;
+          const int tb = t0 + col;  // first time row of this chunk
+          uint32_t r[32];
+          tmem_ld32(taddr + col, r);
+          const int tr = tb + lane;  // lane j looks up row tb + j
+          const unsigned vm =
+              __ballot_sync(0xffffffffu, tr < a.rows_in && a.frame_src[tr / a.out_scale] >= 0);
+          uint8_t* tile = st + (g & 1) * 2048;  // bf16 [32 rows][32 channels], 64-byte swizzle
+          if (lane == 0) bulk_wait_read1();       // the store two chunks back has read this tile
+          __syncwarp();
+          tmem_wait_ld();
+          const uint32_t cbyte = (uint32_t)(lane & 7) * 2;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float v = __uint_as_float(r[j]) + bv;
+            if (!((vm >> j) & 1)) v = 0.f;
+            if (a.alpha) v = snake_inv(v, al, ai);
+            *reinterpret_cast<__nv_bfloat16*>(tile + j * 64 + ((((uint32_t)lane >> 3) ^ ((j >> 1) & 3)) << 4) +
+                                              cbyte) = __float2bfloat16_rn(v);
+          }
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            // rows past the end are clipped by the TMA unit; a chunk wholly past
+            // it commits an empty group so that the tile ring's count holds
+            if (tb < a.rows_out) tma_store_2d(&tmP, smem_u32(tile), 32 * quad, tb);
+            bulk_commit();
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty(buf));
+    }
+    if (lane == 0) bulk_wait0();
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Latent packing and the output head (SIMT: 32 -> 64 columns, 96 -> 1 channel)
 // ---------------------------------------------------------------------------
 
@@ -735,6 +940,39 @@ void launch(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) 
   IRT_CHECK_LAUNCH();
 }
 
+// Transposed narrow dilated convolution (conv_t_kernel).
+void launch_t(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s) {
+  static unsigned attr_mask = 0;
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(attr_mask & (1u << (dev & 31)))) {
+      IRT_CUDA(cudaFuncSetAttribute(conv_t_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)T_SMEM));
+      attr_mask |= 1u << (dev & 31);
+    }
+  }
+  const CUtensorMap ti = tma_map_bf16(in, a.rows_in, a.cin, a.cin, HBOX);
+  const long kcols = (long)a.taps * a.cin_pad;
+  const CUtensorMap tw = tma_map_bf16(w, a.cout, kcols, kcols, a.cout);
+  const CUtensorMap tp = tma_map_tile32(a.p, false, a.rows_out, a.cout, a.cout);
+  const long units = (a.rows_in + NT - 1) / NT;
+  const int grid = (int)std::min<long>(units, num_sms());
+  launch_pdl(conv_t_kernel, dim3(grid), dim3(THREADS), T_SMEM, s, ti, tw, tp, a);
+  IRT_CHECK_LAUNCH();
+}
+
+bool use_conv_t(const ConvTcArgs& a) {
+  static const bool on = [] {
+    const char* e = std::getenv("IRT_CONV_T");
+    return !(e && e[0] == '0');
+  }();
+  return on && !a.convt && a.taps > 1 && !a.add_res && !a.x && a.p && a.cout <= 128 && (a.cout % 32) == 0 &&
+         (a.taps - 1) * a.dil <= T_HALO_MAX && a.rows_out == a.rows_in &&
+         !(reinterpret_cast<uintptr_t>(a.p) & 15);
+}
+
 // Residual stride-1 convolutions take the residual ring, other stride-1
 // convolutions with k > 1 the halo staging (see Cfg).
 template <int BN>
@@ -768,6 +1006,11 @@ void conv_tc(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s)
   // same number of rows (rows_out = rows_in * stride; the even strides)
   ConvTcArgs b = a;
   b.ct_tma = a.convt && !a.add_res && (long)a.rows_out == (long)a.rows_in * a.stride;
+  // narrow k > 1 convolutions (<= 128 output channels): the transposed product
+  if (ctc::use_conv_t(b)) {
+    ctc::launch_t(in, w, b, s);
+    return;
+  }
   switch (conv_tc_bn(a.cout)) {
     case 256: ctc::launch<256>(in, w, b, s); break;
     case 192: ctc::launch<192>(in, w, b, s); break;

@@ -98,6 +98,10 @@ CASES = [
     ("many_k7_d9_c192", 100, 240, 192, 192, 7, 9, 0, 1, 0, True),
     ("many_convt_s10", 2000, 1, 768, 384, 20, 1, 1, 10, 0, True),
     ("many_k7_c768", 40, 480, 768, 768, 7, 1, 0, 1, 0, True),
+    # <= 128 output channels, k > 1: the transposed product (conv_t_kernel)
+    ("many_k7_d9_c96_transposed", 200, 500, 96, 96, 7, 9, 0, 1, 0, True),  # several 256-row units per CTA
+    ("k7_d1_c64_transposed", 50, 30, 64, 64, 7, 1, 0, 1, 0, True),        # half the channel lanes idle
+    ("k7_d3_c96_plain_tail", 40, 37, 96, 96, 7, 3, 0, 1, 0, False),       # no Snake, rows % 256 != 0
 ]
 
 
