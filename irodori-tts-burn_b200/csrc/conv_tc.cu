@@ -417,29 +417,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       if (lane == 0) bulk_wait0();  // every store of this warp has completed
     } else if (!a.convt || a.ct_tma) {
-      // Stride-1 convolutions (output row = GEMM row), and ConvTranspose
-      // phases whose output rows o = q * stride + r leave by 3-D TMA stores
-      // (column, r, q): thread = GEMM row.
-      // Each 32 x 32 chunk leaves through this warp's staging tiles by TMA
-      // stores (f32 residual stream, bf16 Snake output); the residual rows
-      // are read straight into registers (a float4 per 4 columns) one chunk
-      // ahead: the next chunk of the unit while the current one is finished,
-      // and during a unit's last chunk the first chunk of the warp's next
-      // unit (which does not depend on any MMA), so a warp keeps two chunks of
-      // residual rows in flight.  Gap rows are written as exact zeros.
+      // Stride-1 convolutions without a residual (output row = GEMM row), and
+      // ConvTranspose phases whose output rows o = q * stride + r leave by 3-D
+      // TMA stores (column, r, q): thread = GEMM row.  Each 32 x 32 chunk
+      // leaves through this warp's staging tiles by TMA stores (f32 stream,
+      // bf16 Snake output).  Gap rows are written as exact zeros.  (Residual
+      // stride-1 convolutions take the ring path above.)
       uint32_t tl = 0;
-      // residual rows: this lane's row of unit u, columns n0 + c .. + 31
-      auto load_x = [&](int u, int c, float4(&d)[8]) {
-        int mi, ph, ni;
-        unit_coords(u, mi, ph, ni);
-        const int row = mi * BM + quad * 32 + lane;
-        const bool ok = row < a.rows_in;
-        const float4* src = reinterpret_cast<const float4*>(a.x + (long)(ok ? row : 0) * a.cout + ni * BN + c);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) d[k] = ok ? src[k] : make_float4(0.f, 0.f, 0.f, 0.f);
-      };
-      float4 xv[8];
-      if (a.add_res && 32 * half < BN && (int)blockIdx.x < units) load_x(blockIdx.x, 32 * half, xv);
       for (int u = blockIdx.x; u < units; u += gridDim.x, ++tl) {
         int mi, ph, ni;
         unit_coords(u, mi, ph, ni);
@@ -460,12 +444,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int c = 32 * half; c < BN; c += 64) {
           uint32_t r[32];
           tmem_ld32(taddr + c, r);
-          // the residual chunk after this one: this unit's next, or the first
-          // of this warp's next unit
-          const bool in_unit = c + 64 < BN;
-          const bool more = a.add_res && (in_unit || u + (int)gridDim.x < units);
-          float4 xn[8];
-          if (more) load_x(in_unit ? u : u + (int)gridDim.x, in_unit ? c + 64 : 32 * half, xn);
           tmem_wait_ld();
           // the staging tiles: the previous chunk's stores have read them
           uint8_t* xs = slot;         // f32 [32][32], 128-byte swizzle
@@ -484,12 +462,6 @@ __global__ void __launch_bounds__(THREADS, 1)
               const float4 b4 = bp ? reinterpret_cast<const float4*>(bp)[k] : make_float4(0.f, 0.f, 0.f, 0.f);
               float w0 = __uint_as_float(r[4 * k]) + b4.x, w1 = __uint_as_float(r[4 * k + 1]) + b4.y;
               float w2 = __uint_as_float(r[4 * k + 2]) + b4.z, w3 = __uint_as_float(r[4 * k + 3]) + b4.w;
-              if (a.add_res) {
-                w0 += xv[k].x;
-                w1 += xv[k].y;
-                w2 += xv[k].z;
-                w3 += xv[k].w;
-              }
               if (!valid) w0 = w1 = w2 = w3 = 0.f;
               if (a.x)
                 *reinterpret_cast<float4*>(xs + lane * 128 + ((k ^ (lane & 7)) << 4)) = make_float4(w0, w1, w2, w3);
@@ -526,10 +498,6 @@ __global__ void __launch_bounds__(THREADS, 1)
               if (a.p) tma_store_2d(&tmP, smem_u32(ps), n0 + c, q0);
             }
             bulk_commit();
-          }
-          if (more) {
-#pragma unroll
-            for (int k = 0; k < 8; ++k) xv[k] = xn[k];
           }
         }
         tc_fence_before();
@@ -996,6 +964,7 @@ void conv_tc(const bf16* in, const bf16* w, const ConvTcArgs& a, cudaStream_t s)
   if ((reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
     throw unsupported("conv_tc: operands must be 16-byte aligned");
   if (a.alpha && !a.alpha_inv) throw Error(IRT_E_INVALID_ARG, "conv_tc: Snake alpha needs its reciprocal table");
+  if (a.add_res && !a.x) throw Error(IRT_E_INVALID_ARG, "conv_tc: a residual convolution needs its f32 stream x");
   if ((a.x && (reinterpret_cast<uintptr_t>(a.x) & 15)) || (a.p && (reinterpret_cast<uintptr_t>(a.p) & 15)) ||
       (a.bias && (reinterpret_cast<uintptr_t>(a.bias) & 15)) ||
       (a.alpha && ((reinterpret_cast<uintptr_t>(a.alpha) | reinterpret_cast<uintptr_t>(a.alpha_inv)) & 15)))
