@@ -149,12 +149,22 @@ __global__ void __launch_bounds__(NT) rownorm_reg_kernel(const float* __restrict
   }
 }
 
+// Up to this many rows the row kernels run 256 threads x 2 float4 per row:
+// at the config-3 sizes (750-1,500 rows) each launch is latency-bound, and the
+// row kernels' share of the request's critical path (CUPTI trace) measured
+// 10.7 ms against 12.3 ms for 128 x 4 (11.3 for 512 x 1, 24.4 for one warp per
+// row); above it 128 x 4, the faster one on bandwidth.
+constexpr int RN_SMALL_M = 8192;
+
 void rownorm(const float* x, const float* a, const float* b, void* y, int out_bf16, int M, int D, float eps, int mode,
              cudaStream_t s) {
   if (M <= 0) return;
   // 128 threads x 4 float4 per row (rows up to D = 2048 held in registers):
   // measured 6.6 TB/s at 54,504 rows of 2048 against 5.9 TB/s for 256 x 2
-  if ((D % 4) == 0 && D / 4 <= 128 * 4) {
+  if ((D % 4) == 0 && D / 4 <= 256 * 2 && M <= RN_SMALL_M) {
+    if (out_bf16) launch_pdl(rownorm_reg_kernel<256, 2, true>, dim3(M), dim3(256), 0, s, x, a, b, y, D, eps, mode);
+    else launch_pdl(rownorm_reg_kernel<256, 2, false>, dim3(M), dim3(256), 0, s, x, a, b, y, D, eps, mode);
+  } else if ((D % 4) == 0 && D / 4 <= 128 * 4) {
     if (out_bf16) launch_pdl(rownorm_reg_kernel<128, 4, true>, dim3(M), dim3(128), 0, s, x, a, b, y, D, eps, mode);
     else launch_pdl(rownorm_reg_kernel<128, 4, false>, dim3(M), dim3(128), 0, s, x, a, b, y, D, eps, mode);
   } else if (out_bf16) {
@@ -405,8 +415,12 @@ bool rms_norm_split_supported(int D) { return D % 4 == 0 && D / 4 <= 128 * 4; }
 void rms_norm_split(const float* x, const float* w, bf16* y, int M, int D, float eps, cudaStream_t s) {
   if (M <= 0) return;
   if (!rms_norm_split_supported(D)) throw unsupported("rms_norm_split: D must be a multiple of 4 and <= 2048");
-  launch_pdl(rownorm_reg_kernel<128, 4, true, true>, dim3(M), dim3(128), 0, s, x, w, (const float*)nullptr,
-             (void*)y, D, eps, 0);
+  if (M <= RN_SMALL_M)
+    launch_pdl(rownorm_reg_kernel<256, 2, true, true>, dim3(M), dim3(256), 0, s, x, w, (const float*)nullptr,
+               (void*)y, D, eps, 0);
+  else
+    launch_pdl(rownorm_reg_kernel<128, 4, true, true>, dim3(M), dim3(128), 0, s, x, w, (const float*)nullptr,
+               (void*)y, D, eps, 0);
   IRT_CHECK_LAUNCH();
 }
 void rmsnorm_proj(const float* x, const float* nw, const void* W, int w_bf16, const float* bias, float* out, int M,
