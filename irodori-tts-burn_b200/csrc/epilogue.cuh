@@ -163,9 +163,10 @@ __device__ __forceinline__ void epi_head(const EpiParams& p, int m, int n0, cons
     int head = col / hd;
     idx = (long)m * Dq + col;
     dst = which == 0 ? p.q : which == 1 ? p.k : which == 2 ? p.v : p.g;
-    if (which == 0) nw = p.qn_w + col;
-    if (which == 1) nw = p.kn_w + col;
-    if (which < 2 && head < p.rope_heads) { rope = 1; pos = p.tok_pos ? p.tok_pos[m] : m; }
+    // no weights (null) means no head norm; offset only a real table
+    if (which == 0 && p.qn_w) nw = p.qn_w + col;
+    if (which == 1 && p.kn_w) nw = p.kn_w + col;
+    if (which < 2 && head < p.rope_heads && p.rope_cos && p.rope_sin) { rope = 1; pos = p.tok_pos ? p.tok_pos[m] : m; }
     act_sig = which == 3;
   } else {  // EPI_CTXKV
     int dr = p.row_map ? p.row_map[m] : m;
@@ -176,7 +177,7 @@ __device__ __forceinline__ void epi_head(const EpiParams& p, int m, int n0, cons
     int col = r - part * Dq;
     idx = (long)l * p.layer_stride + (long)dr * Dq + col;
     dst = part == 0 ? p.ck : p.cv;
-    if (part == 0) nw = p.kn_w + (long)l * Dq + col;
+    if (part == 0 && p.kn_w) nw = p.kn_w + (long)l * Dq + col;
   }
   float rms = 1.f;
   if (nw) {
@@ -261,8 +262,9 @@ __device__ __forceinline__ void epi_head_staged(const EpiParams& p, int m_base, 
   const int col = n0 - which * Dq;
   const int head = col / HD;
   bf16* dst = reinterpret_cast<bf16*>(which == 0 ? p.q : which == 1 ? p.k : which == 2 ? p.v : p.g);
-  const float* nw = which == 0 ? p.qn_w + col : which == 1 ? p.kn_w + col : nullptr;
-  const bool rope = which < 2 && head < p.rope_heads;
+  // no weights (null) means no head norm; offset only a real table
+  const float* nw = (which == 0 && p.qn_w) ? p.qn_w + col : (which == 1 && p.kn_w) ? p.kn_w + col : nullptr;
+  const bool rope = which < 2 && head < p.rope_heads && p.rope_cos && p.rope_sin;
   const bool act_sig = which == 3;
   const int m = m_base + lane;
   const int mc = m < M ? m : M - 1;  // table lookups stay in bounds for rows past M

@@ -114,6 +114,26 @@ def test_gemm_qkvg_epilogue(dev, path):
         assert err < 1e-2, f"{name}: rel err {err}"
 
 
+@pytest.mark.parametrize("path", [0, 1])
+def test_gemm_qkvg_without_norm_weights_or_rope(dev, path):
+    """Null head-norm weights mean no head norm and no RoPE tables mean no
+    RoPE: q / k / v are the plain projections, g its sigmoid (the epilogue
+    must not offset a null weight pointer)."""
+    M, H, hd = 300, 4, 128
+    D = H * hd
+    g = torch.Generator(device=dev).manual_seed(12)
+    A = torch.randn(M, D, device=dev, generator=g).to(torch.bfloat16)
+    W = (torch.randn(4 * D, D, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    outs = [torch.zeros(M, D, device=dev, dtype=torch.bfloat16) for _ in range(4)]
+    check(hooks().irtt_gemm_epi(1, ptr(A), ptr(W), M, 4 * D, D, path, *[ptr(o) for o in outs], None, None, None,
+                                None, None, H, hd, H // 2, None, None, 0))
+    acc = A.float() @ W.float().T
+    q, k, v, gg = acc.split(D, dim=1)
+    for o, r, name in zip(outs, [q, k, v, torch.sigmoid(gg)], "qkvg"):
+        err = (o.float() - r).abs().max().item() / r.abs().max().item()
+        assert err < 1e-2, f"{name}: rel err {err}"
+
+
 # (M, N, K, batch, bf16 operands, A row pitch, A batch stride): the engine's
 # adaLN-table and cond_module shapes (one row per timestep), tails in every
 # dimension, the scalar-load path (K % 4 != 0, bf16) and the cluster K-split
