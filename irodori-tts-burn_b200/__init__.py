@@ -277,7 +277,9 @@ def _as_buffer(x, dtype: str, keep: list):
     if torch is not None and isinstance(x, torch.Tensor):
         tdt = {"int32": torch.int32, "uint8": torch.uint8, "float32": torch.float32}[dtype]
         if x.dtype == torch.bool:
-            x = x.to(torch.uint8)
+            # one byte per element holding 0 / 1: the same buffer as uint8, no
+            # conversion kernel on the device
+            x = x.contiguous().view(torch.uint8)
         t = x.to(tdt).contiguous()
         keep.append(t)
         return t.data_ptr(), tuple(t.shape), t.is_cuda
