@@ -386,8 +386,10 @@ def attn_case(steps, which="c3"):
     context keys; uncond row: 750 over 750).  "c4": the config-4 CFG step
     (64 utterances; cond rows over self + text + speaker keys, uncond rows over
     self keys), packed (group, utterance, frame) like the engine.  "c4p" /
-    "c3p": the config-4 / config-3 plain step (cond rows only).  Returns (ms
-    per launch, TFLOP/s)."""
+    "c3p": the config-4 / config-3 plain step (cond rows only).  "c3f" / "c3w":
+    the config-3 CFG step in f32 storage through the register-tiled SIMT
+    kernel / the warp-per-query SIMT kernel.  Returns (ms per launch,
+    TFLOP/s)."""
     import torch
     L = ctypes.CDLL(str(PKG_DIR / "libirodori_b200_testhooks.so"))
     L.irtt_attention.argtypes = ([ctypes.c_void_p] * 8 + [ctypes.c_int] * 3 + [ctypes.c_void_p] + [ctypes.c_int] * 4)
@@ -403,6 +405,9 @@ def attn_case(steps, which="c3"):
     else:
         lens, ctxs = [750], [576]
     uncond = which not in ("c4p", "c3p")
+    f32 = which in ("c3f", "c3w")
+    dt = torch.float32 if f32 else torch.bfloat16
+    path = {"c3f": 2, "c3w": 3}.get(which, 0)
     seqs, tok, co = [], 0, 0
     for S, c in zip(lens, ctxs):  # cond rows
         seqs.append((tok, S, co, c))
@@ -412,17 +417,17 @@ def attn_case(steps, which="c3"):
         tok += S
     rows, C = tok, co
     g = torch.Generator(device=dev).manual_seed(0)
-    mk = lambda m: torch.randn(m, D, device=dev, generator=g).to(torch.bfloat16)  # noqa: E731
+    mk = lambda m: torch.randn(m, D, device=dev, generator=g).to(dt)  # noqa: E731
     q, k, v, ck_, cv = mk(rows), mk(rows), mk(rows), mk(max(C, 128)), mk(max(C, 128))
-    gs = torch.sigmoid(torch.randn(rows, D, device=dev, generator=g)).to(torch.bfloat16)
-    out = torch.empty(rows, D, device=dev, dtype=torch.bfloat16)
+    gs = torch.sigmoid(torch.randn(rows, D, device=dev, generator=g)).to(dt)
+    out = torch.empty(rows, D, device=dev, dtype=dt)
     sd = (ctypes.c_int * (4 * len(seqs)))(*[x for t in seqs for x in t])
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
     flops = sum(4 * S * (S + c) * D + (4 * S * S * D if uncond else 0) for S, c in zip(lens, ctxs))
 
     def launch():
-        rc = L.irtt_attention_async(P(q), P(k), P(v), P(gs), P(ck_), P(cv), None, sd, len(seqs), H, hd, P(out), 1,
-                                    rows, max(C, 128), 0)
+        rc = L.irtt_attention_async(P(q), P(k), P(v), P(gs), P(ck_), P(cv), None, sd, len(seqs), H, hd, P(out),
+                                    0 if f32 else 1, rows, max(C, 128), path)
         if rc:
             raise RuntimeError(L.irtt_last_error().decode())
 
@@ -665,9 +670,11 @@ def main():
     ap.add_argument("--codec-precision", default="bf16", choices=["bf16", "f32"])
     ap.add_argument("--codec-utts", type=int, default=16,
                     help="with --codec-only: decode the first N of the 16 config-5 utterances (profiling case)")
-    ap.add_argument("--attn-case", nargs="?", const="c3", default=None, choices=["c3", "c3p", "c4", "c4p"],
+    ap.add_argument("--attn-case", nargs="?", const="c3", default=None,
+                    choices=["c3", "c3p", "c4", "c4p", "c3f", "c3w"],
                     help="only the joint attention of one layer: config-3 CFG step (c3), config-4 CFG step (c4) "
-                         "or config-4 plain step (c4p), --steps launches (profiling case)")
+                         "or config-4 plain step (c4p); c3f / c3w: config-3 CFG step in f32 (register-tiled / "
+                         "warp-per-query SIMT kernel); --steps launches (profiling case)")
     ap.add_argument("--ckpt", default=None)
     ap.add_argument("--row-case", type=int, default=0,
                     help="profiling case: the adaLN modulate row kernel alone at M rows, --steps launches")

@@ -8,6 +8,8 @@
 // attn_mma_kernel: bf16 operands, f32 online softmax, mma.sync m16n8k16,
 //   64 queries x 1 head per CTA (4 warps x 16 rows), 64-key tiles double-
 //   buffered with cp.async, XOR-swizzled shared memory, hd = 128.
+// attn_simt_tiled_kernel: f32 storage, hd = 128, 64 queries x 1 head per CTA,
+//   register-tiled scores and output (the f32 parity mode's attention).
 // attn_simt_kernel: any even hd, f32 or bf16 storage, one warp per (query, head).
 #include "common.hpp"
 #include "kernels.hpp"
@@ -138,6 +140,221 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+
+// ---------------------------------------------------------------------------
+// Register-tiled SIMT kernel (f32 storage, hd = 128)
+//
+// One CTA = 64 queries x 1 head, 256 threads, 64-key tiles.  Thread (r, c) with
+// r = warp * 2 + lane / 16 and c = lane % 16 owns query rows r + 16 i (i < 4):
+// the scores of keys c + 16 j (j < 4) and the output columns 4c..4c+3 and
+// 64+4c..64+4c+3.  A row's 64 scores of a tile live in one half-warp, so the
+// tile's row maximum and the online-softmax correction come from shuffles and
+// stay in the registers of the threads that rescale that row's output.
+// Shared memory: Q, K as [row][128] with 16-byte chunks XOR-swizzled by row
+// (conflict-free column reads across rows), V plain, the probabilities
+// transposed [key][4 rows of a thread] with chunks swizzled by key.  K of tile
+// t+1 loads (cp.async) during tile t's softmax and P.V, V of tile t+1 during
+// tile t+1's scores.  Invalid keys (past the sequence, masked) are zero-filled
+// in K and V and scored -inf.  Two CTAs fit per SM.
+// ---------------------------------------------------------------------------
+constexpr int FQ = 64, FK = 64, FHD = 128;
+constexpr int F_SMEM = (FQ * FHD + 2 * FK * FHD + FK * FQ) * 4 + FK * 4;
+
+__global__ void __launch_bounds__(256, 2) attn_simt_tiled_kernel(AttnParams p) {
+  extern __shared__ __align__(16) float fsm[];
+  float* sq = fsm;                  // [64][128], chunk c of row r at c ^ (r & 7)
+  float* sk = sq + FQ * FHD;        // [64][128], same swizzle
+  float* sv = sk + FK * FHD;        // [64][128]
+  float* sp = sv + FK * FHD;        // [64 keys][16 chunks of 4 rows], chunk r at r ^ (key & 15)
+  float* kbias = sp + FK * FQ;      // [64] 0 (valid key) or -inf
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int r = warp * 2 + lane / 16, c = lane % 16;
+  const int h = blockIdx.y;
+  const SeqDesc sd = p.seqs[blockIdx.z];
+  const int q0 = blockIdx.x * FQ;
+  if (q0 >= sd.len) return;
+  const int D = p.H * FHD;
+  const float* Q = reinterpret_cast<const float*>(p.q);
+  const float* K = reinterpret_cast<const float*>(p.k);
+  const float* V = reinterpret_cast<const float*>(p.v);
+  const float* CK = reinterpret_cast<const float*>(p.ck);
+  const float* CV = reinterpret_cast<const float*>(p.cv);
+  const int nk = sd.len + sd.ctx_len;
+  const int ntiles = (nk + FK - 1) / FK;
+  const uint32_t sq_u = (uint32_t)__cvta_generic_to_shared(sq);
+  const uint32_t sk_u = (uint32_t)__cvta_generic_to_shared(sk);
+  const uint32_t sv_u = (uint32_t)__cvta_generic_to_shared(sv);
+
+  // Tile loaders: 64 rows x 32 chunks = 8 chunks per thread, coalesced rows.
+  auto key_row = [&](int j, bool& ctx, long& row, bool& valid) {
+    ctx = j >= sd.len;
+    if (!ctx) {
+      row = (long)(sd.tok_start + j);
+      valid = !p.key_mask || p.key_mask[row];
+    } else {
+      row = (long)(sd.ctx_off + j - sd.len);
+      valid = j < nk;
+    }
+  };
+  auto load_keys = [&](int t, bool values) {
+    const uint32_t dst_u = values ? sv_u : sk_u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int id = tid + 256 * i, rr = id / 32, ch = id % 32;
+      bool ctx, valid;
+      long row;
+      key_row(t * FK + rr, ctx, row, valid);
+      const float* src = values ? V : K;  // zero-fill when invalid: not read
+      if (valid) src = (ctx ? (values ? CV : CK) : src) + row * D + h * FHD + ch * 4;
+      const int dch = values ? ch : (ch ^ (rr & 7));
+      cp_async16(dst_u + (uint32_t)(rr * FHD + dch * 4) * 4, src, valid);
+      if (!values && ch == 0) kbias[rr] = valid ? 0.f : -INFINITY;
+    }
+  };
+
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int id = tid + 256 * i, rr = id / 32, ch = id % 32;
+    const bool valid = q0 + rr < sd.len;
+    const float* src = valid ? Q + (long)(sd.tok_start + q0 + rr) * D + h * FHD + ch * 4 : Q;
+    cp_async16(sq_u + (uint32_t)(rr * FHD + (ch ^ (rr & 7)) * 4) * 4, src, valid);
+  }
+  load_keys(0, false);
+  cp_commit();
+  load_keys(0, true);
+  cp_commit();
+
+  float acc[4][8];
+  float m[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int d = 0; d < 8; ++d) acc[i][d] = 0.f;
+  }
+
+  for (int t = 0; t < ntiles; ++t) {
+    cp_wait<1>();  // Q and K of this tile
+    __syncthreads();
+    float s[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+    const float4* q4 = reinterpret_cast<const float4*>(sq);
+    const float4* k4 = reinterpret_cast<const float4*>(sk);
+#pragma unroll 4
+    for (int ch = 0; ch < 32; ++ch) {
+      float4 qa[4], kb[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) qa[i] = q4[(r + 16 * i) * 32 + (ch ^ (r & 7))];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kb[j] = k4[(c + 16 * j) * 32 + (ch ^ (c & 7))];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          s[i][j] = fmaf(qa[i].x, kb[j].x, s[i][j]);
+          s[i][j] = fmaf(qa[i].y, kb[j].y, s[i][j]);
+          s[i][j] = fmaf(qa[i].z, kb[j].z, s[i][j]);
+          s[i][j] = fmaf(qa[i].w, kb[j].w, s[i][j]);
+        }
+    }
+    float bias[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bias[j] = kbias[c + 16 * j];
+    __syncthreads();  // every thread is done with K (and the bias) of this tile
+    if (t + 1 < ntiles) load_keys(t + 1, false);
+    cp_commit();
+
+    // online softmax, one row per (i, half-warp)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s[i][j] = s[i][j] * p.scale + bias[j];
+        mx = fmaxf(mx, s[i][j]);
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mn = fmaxf(m[i], mx);
+      float corr = 1.f, sum = 0.f;
+      if (mn != -INFINITY) {
+        corr = expf(m[i] - mn);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          s[i][j] = expf(s[i][j] - mn);
+          sum += s[i][j];
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+      }
+      m[i] = mn;
+      l[i] = l[i] * corr + sum;
+#pragma unroll
+      for (int d = 0; d < 8; ++d) acc[i][d] *= corr;
+    }
+    float4* p4 = reinterpret_cast<float4*>(sp);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int key = c + 16 * j;
+      p4[key * 16 + (r ^ (key & 15))] = make_float4(s[0][j], s[1][j], s[2][j], s[3][j]);
+    }
+    if (t + 1 < ntiles) cp_wait<1>();  // V of this tile (K of the next may still fly)
+    else cp_wait<0>();
+    __syncthreads();
+    const float4* v4 = reinterpret_cast<const float4*>(sv);
+#pragma unroll 4
+    for (int key = 0; key < FK; ++key) {
+      const float4 pr = p4[key * 16 + (r ^ (key & 15))];
+      const float4 va = v4[key * 32 + c], vb = v4[key * 32 + 16 + c];
+      const float pv[4] = {pr.x, pr.y, pr.z, pr.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[i][0] = fmaf(pv[i], va.x, acc[i][0]);
+        acc[i][1] = fmaf(pv[i], va.y, acc[i][1]);
+        acc[i][2] = fmaf(pv[i], va.z, acc[i][2]);
+        acc[i][3] = fmaf(pv[i], va.w, acc[i][3]);
+        acc[i][4] = fmaf(pv[i], vb.x, acc[i][4]);
+        acc[i][5] = fmaf(pv[i], vb.y, acc[i][5]);
+        acc[i][6] = fmaf(pv[i], vb.z, acc[i][6]);
+        acc[i][7] = fmaf(pv[i], vb.w, acc[i][7]);
+      }
+    }
+    __syncthreads();  // every thread is done with V and P of this tile
+    if (t + 1 < ntiles) load_keys(t + 1, true);
+    cp_commit();
+  }
+  cp_wait<0>();
+
+  float* out = reinterpret_cast<float*>(p.out);
+  const float* G = reinterpret_cast<const float*>(p.gsig);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float lt = l[i];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o);
+    const int qi = q0 + r + 16 * i;
+    if (qi >= sd.len) continue;
+    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+    const long off = (long)(sd.tok_start + qi) * D + h * FHD;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int d = half * 64 + 4 * c;
+      float4 o = make_float4(acc[i][4 * half] * inv, acc[i][4 * half + 1] * inv, acc[i][4 * half + 2] * inv,
+                             acc[i][4 * half + 3] * inv);
+      if (G) {
+        const float4 g = *reinterpret_cast<const float4*>(G + off + d);
+        o.x *= g.x; o.y *= g.y; o.z *= g.z; o.w *= g.w;
+      }
+      *reinterpret_cast<float4*>(out + off + d) = o;
+    }
+  }
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&t);
@@ -349,6 +566,16 @@ void attention(const AttnParams& p, int bf16_io, cudaStream_t s) {
     }
     dim3 grid((p.max_len + QT - 1) / QT, p.H, p.nseq);
     attn_mma_kernel<<<grid, 128, smem, s>>>(p);
+  } else if (!bf16_io && p.hd == FHD && p.path != 3) {
+    static int attr_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (attr_dev != dev) {
+      IRT_CUDA(cudaFuncSetAttribute(attn_simt_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, F_SMEM));
+      attr_dev = dev;
+    }
+    dim3 grid((p.max_len + FQ - 1) / FQ, p.H, p.nseq);
+    attn_simt_tiled_kernel<<<grid, 256, F_SMEM, s>>>(p);
   } else {
     if (p.hd > 256) throw unsupported("attention head_dim > 256");
     dim3 grid((p.max_len + 3) / 4, p.H, p.nseq);

@@ -112,7 +112,8 @@ struct AttnParams {
   void* out;          // [M, H*hd]
   int rows;           // rows of the q/k/v buffers (TMA bounds)
   int ctx_rows;       // rows of the context cache (TMA bounds)
-  int path;           // 0 = best available, 1 = mma.sync kernel, 2 = SIMT kernel
+  int path;           // 0 = best available, 1 = mma.sync kernel, 2 = SIMT kernel (register-tiled
+                      // for f32 at hd = 128), 3 = warp-per-query SIMT kernel
 };
 void attention(const AttnParams& p, int bf16_io, cudaStream_t s);
 bool attention_tc_supported(const AttnParams& p);

@@ -269,7 +269,7 @@ def _attn_ref(q, k, v, g, ck, cv, key_mask, seqs, H, hd):
     return out
 
 
-ATTN_PATHS = [(1, 0), (1, 1), (0, 2)]  # (bf16, path): tcgen05, mma.sync, SIMT
+ATTN_PATHS = [(1, 0), (1, 1), (0, 2), (0, 3)]  # (bf16, path): tcgen05, mma.sync, tiled SIMT, warp SIMT
 
 
 @pytest.mark.parametrize("kt", ["64", "128"])
@@ -317,7 +317,7 @@ def test_attention_matches_torch(dev, bf16, path, case):
     assert err < (2e-2 if bf16 else 1e-5), f"attention rel err {err}"
 
 
-@pytest.mark.parametrize("bf16,path", [(1, 1), (0, 2)])
+@pytest.mark.parametrize("bf16,path", [(1, 1), (0, 2), (0, 3)])
 def test_attention_key_mask_and_empty_rows(dev, bf16, path):
     """Masked self keys are skipped; a sequence whose keys are all masked
     yields exactly 0 (safe softmax), even with NaN in the masked V rows."""
