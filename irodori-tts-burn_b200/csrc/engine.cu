@@ -101,6 +101,43 @@ Engine::Engine(int dev, const std::string& path, int precision, const std::strin
   IRT_CUDA(cudaSetDevice(dev));
   IRT_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   load(path, adapter_dir);
+  const char* simt = std::getenv("IRT_F32_SIMT");
+  tf32 = !bf && !(simt && simt[0] == '1');
+  if (tf32) prepare_tf32();
+}
+
+// f32 mode: the tf32 hi / lo copy of each GEMM weight that can meet 128 or
+// more rows (encoder blocks and in_proj, DiT blocks and in_proj, context KV
+// projections; the cond_module runs on one row per timestep and stays SIMT).
+// Built after the adapter merge, from the merged weights.
+void Engine::prepare_tf32() {
+  auto add = [&](const DevBuf& W, int N, int K) {
+    if (!W.p || N <= 0 || K <= 0 || (K % 4)) return;
+    const int Kp = tf32_kpad(K);
+    DevBuf b((size_t)N * 2 * Kp * 4);
+    split_tf32(W.as<float>(), K, N, K, b.as<float>(), Kp, stream);
+    w_tf32.emplace(W.p, std::move(b));
+  };
+  for (EncoderW* e : {&text_enc, &aux_enc}) {
+    if (!e->dim) continue;
+    if (e->in_dim > 0) add(e->in_w, e->dim, e->in_dim);
+    for (auto& b : e->blk) {
+      add(b.wqkvg, 4 * e->dim, e->dim);
+      add(b.wo, e->dim, e->dim);
+      add(b.w13, 2 * e->Fp, e->dim);
+      add(b.w2, e->dim, e->F);
+    }
+  }
+  add(in_w, D, Kin);
+  for (auto& b : blk) {
+    add(b.wqkvg, 4 * D, D);
+    add(b.wo, D, D);
+    add(b.w13, 2 * Fp, D);
+    add(b.w2, D, F);
+  }
+  if (ctx_text_w.p) add(ctx_text_w, L * 2 * D, (int)cfg.text_dim);
+  if (ctx_aux_w.p && aux_dim > 0) add(ctx_aux_w, L * 2 * D, aux_dim);
+  IRT_CUDA(cudaStreamSynchronize(stream));
 }
 
 Engine::~Engine() {
@@ -338,6 +375,17 @@ void Engine::gemm(const void* A, long lda, const DevBuf& W, int M, int N, int K,
     gemm_tc(reinterpret_cast<const bf16*>(A), lda, W.as<bf16>(), K, M, N, K, p, s);
     return;
   }
+  if (tf32) {
+    const auto it = w_tf32.find(W.p);
+    const int Kp = tf32_kpad(K);
+    if (it != w_tf32.end() && (lda % 4) == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0 &&
+        gemm_tc_supported(p, Kp, 2L * Kp, 2L * Kp, A, it->second.p)) {
+      ws.a2.ensure((size_t)M * 2 * Kp * 4);
+      split_tf32(static_cast<const float*>(A), lda, M, K, ws.a2.as<float>(), Kp, s);
+      gemm_tc_tf32x3(ws.a2.as<float>(), 2L * Kp, it->second.as<float>(), 2L * Kp, M, N, Kp, p, s);
+      return;
+    }
+  }
   ws.raw.ensure((size_t)M * N * 4);
   gemm_simt(A, bf, lda, 0, W.p, bf, K, 0, ws.raw.as<float>(), N, 0, M, N, K, 1, s);
   epilogue_apply(p, ws.raw.as<float>(), N, 0, 1, s);
@@ -459,7 +507,7 @@ void Engine::forward_step(int M, const SeqDesc* d_seqs, int nseq, int max_len, i
       (uintptr_t)ws.x.p, (uintptr_t)ws.h.p, (uintptr_t)ws.q.p, (uintptr_t)ws.k.p, (uintptr_t)ws.v.p,
       (uintptr_t)ws.g.p, (uintptr_t)ws.attn.p, (uintptr_t)ws.hm.p, (uintptr_t)ws.xin.p, (uintptr_t)ws.vout.p,
       (uintptr_t)ws.raw.p, (uintptr_t)ws.tokpos.p, (uintptr_t)ws.cache_k.p, (uintptr_t)ws.cache_v.p,
-      (uintptr_t)ws.rope_cos.p, (uintptr_t)ws.rope_sin.p, (uintptr_t)ada_cur.p};
+      (uintptr_t)ws.rope_cos.p, (uintptr_t)ws.rope_sin.p, (uintptr_t)ada_cur.p, (uintptr_t)ws.a2.p};
   auto it = graphs.find(key);
   if (it == graphs.end()) {
     // keys seen once and never again (a server sees many ragged shapes) must

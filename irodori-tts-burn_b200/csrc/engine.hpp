@@ -7,6 +7,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "common.hpp"
@@ -73,6 +74,12 @@ struct Engine {
   // normalised rows runs on the tcgen05 GEMM (only the first P columns are
   // stored)
   DevBuf out_w_pad;
+  // f32 mode: [W_hi | W_lo] ([N, 2 Kp], tf32 hi / lo halves) of every GEMM
+  // weight that meets 128 or more rows, keyed by the f32 weight's address;
+  // such GEMMs run on the tcgen05 tf32 path (gemm_tc_tf32x3) instead of the
+  // SIMT kernel.  IRT_F32_SIMT=1 keeps every f32 GEMM on the SIMT kernel.
+  bool tf32 = false;
+  std::unordered_map<const void*, DevBuf> w_tf32;
 
   // workspaces (grow-only)
   struct WS {
@@ -83,6 +90,7 @@ struct Engine {
     DevBuf ids, tmask, ref, rmask, cids, cmask, noise, out;
     DevBuf rope_cos, rope_sin;
     DevBuf text_t, lat_t, st2, amask_in, amaskf, h0, h1, uo, ul, rows;
+    DevBuf a2;  // f32 mode: [A_hi | A_lo] of the current GEMM operand
   } ws;
 
   long long last_row_forwards = 0, last_launches = 0;
@@ -123,6 +131,7 @@ struct Engine {
 
  private:
   void load(const std::string& path, const std::string& adapter_dir);
+  void prepare_tf32();
   void load_encoder(const SafeTensorsFile& st, EncoderW& e, const std::string& prefix, int dim, int heads,
                     int layers, double ratio, bool embedding, int vocab, int in_dim);
 };

@@ -41,6 +41,9 @@ namespace tc {
 constexpr int BM = 128, BK = 64, EPI_WARPS = 8, THREADS = 64 + 32 * EPI_WARPS;
 // Smallest k-block span of a group in a tail split (splits == -2).
 constexpr int TAIL_MIN_SPAN = 8;
+// TF: k-blocks per accumulator chunk (each chunk's MMA chain restarts at 0
+// and is added into the tile sum by the epilogue warps).
+constexpr int TF_CHUNK = 8;
 constexpr uint32_t A_BYTES = BM * BK * 2;
 
 // CG = CTAs per MMA: 1, or 2 for a CTA pair (cluster of 2) that computes a
@@ -64,6 +67,9 @@ struct Cfg {
   // both, N>>3 at bits 17-22, M>>4 at bits 24-28 (M = 128 per CTA of the group).
   static constexpr uint32_t IDESC =
       (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)((BM * CG) >> 4) << 24);
+  // kind::tf32 (the f32 mode's split product, TF below): same tile bytes, 32
+  // f32 per 128-byte row instead of 64 bf16.
+  static constexpr uint32_t IDESC_TF = tcx::idesc_tf32(BM * CG, BN);
 };
 
 // The sm_100a helper layer (mbarriers with the bounded wait, TMA, UMMA
@@ -168,7 +174,13 @@ struct Regs {
 // much as 12 and the kernel must stay at or below 168 registers per thread.
 // CG = 2: launched as clusters of 2 CTAs (consecutive blockIdx.x); the pair
 // walks the same work units, rank 0 issues the MMAs for both.
-template <int BN, int CG>
+// TF: f32 operands as tf32 hi / lo pairs (the f32 mode).  A = [A_hi | A_lo]
+// [M, 2K] and B = [B_hi | B_lo] [N, 2K] (K a multiple of 32); the k-blocks run
+// over three segments of K / 32 blocks each -- A_hi.B_hi, A_hi.B_lo, A_lo.B_hi
+// -- into one f32 accumulator, so the product keeps about f32 accuracy
+// (the dropped A_lo.B_lo term and the tf32 reading of the lo halves are
+// ~2^-22 of each product) at the tf32 tensor rate.
+template <int BN, int CG, bool TF>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmX, int M, int N, int K, int splits,
@@ -176,6 +188,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   using C = Cfg<BN, CG>;
   constexpr int STAGES = C::STAGES;
   constexpr int BMT = BM * CG;  // rows of one work tile
+  // TF: two accumulator buffers + two tile sums (see the epilogue), BN = 128
+  static_assert(!TF || BN == 128, "the tf32 path runs 128-column tiles");
+  constexpr uint32_t TMEM_COLS = TF ? 4 * BN : C::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
@@ -188,7 +203,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int grp0 = blockIdx.x / CG, ngrp = gridDim.x / CG;  // work-group index and count
   const int m_tiles = (M + BMT - 1) / BMT, n_tiles = (N + BN - 1) / BN;
   const int num_tiles = m_tiles * n_tiles;
-  const int k_blocks = (K + BK - 1) / BK;
+  const int k_blocks = TF ? 3 * (K / 32) : (K + BK - 1) / BK;
   // work units: see Units (splits != 1 only for the additive RESID epilogue)
   const Units units(grp0, ngrp, num_tiles, k_blocks, splits, TAIL_MIN_SPAN);
 
@@ -215,11 +230,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     if constexpr (CG == 2) {
       // executed by one warp in each CTA of the pair: same columns in both
       asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                   "r"(C::TMEM_COLS));
+                   "r"(TMEM_COLS));
       asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
     } else {
       asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                   "r"(C::TMEM_COLS));
+                   "r"(TMEM_COLS));
       asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
   }
@@ -248,17 +263,23 @@ __global__ void __launch_bounds__(THREADS, 1)
           mbar_wait(empty(s), ph ^ 1);
           uint8_t* a_dst = tiles + s * C::STAGE_BYTES;
           uint8_t* b_dst = a_dst + A_BYTES;
+          int ca = kb * BK, cb = kb * BK;  // element columns of the A and B boxes
+          if constexpr (TF) {
+            const int kseg = K / 32, seg = kb / kseg, kk = (kb - seg * kseg) * 32;
+            ca = (seg == 2 ? K : 0) + kk;
+            cb = (seg == 1 ? K : 0) + kk;
+          }
           if constexpr (CG == 2) {
             // both CTAs' copies complete on rank 0's full barrier, which
             // expects the pair's bytes
             const uint32_t fb = map_rank0(full(s));
             if (rank == 0) mbar_expect_tx(full(s), CG * C::STAGE_BYTES);
-            tma_load_2d_pair(smem_u32(a_dst), &tmA, fb, kb * BK, m0);
-            tma_load_2d_pair(smem_u32(b_dst), &tmB, fb, kb * BK, n0);
+            tma_load_2d_pair(smem_u32(a_dst), &tmA, fb, ca, m0);
+            tma_load_2d_pair(smem_u32(b_dst), &tmB, fb, cb, n0);
           } else {
             mbar_expect_tx(full(s), C::STAGE_BYTES);
-            tma_load_2d(smem_u32(a_dst), &tmA, full(s), kb * BK, m0);
-            tma_load_2d(smem_u32(b_dst), &tmB, full(s), kb * BK, n0);
+            tma_load_2d(smem_u32(a_dst), &tmA, full(s), ca, m0);
+            tma_load_2d(smem_u32(b_dst), &tmB, full(s), cb, n0);
           }
         }
       }
@@ -268,6 +289,40 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0 && rank == 0) {
       uint32_t it = 0, tl = 0;
       int t, kb0, kb1;
+      if constexpr (TF) {
+        // accumulation chunks of TF_CHUNK k-blocks, alternating between the
+        // two accumulator buffers (tl counts chunks here)
+        for (int i = 0; units.get(i, t, kb0, kb1); ++i) {
+          for (int c0 = kb0; c0 < kb1; c0 += TF_CHUNK, ++tl) {
+            const int c1 = min(kb1, c0 + TF_CHUNK);
+            const int buf = tl & 1;
+            const uint32_t aph = (tl >> 1) & 1;
+            mbar_wait(tempty(buf), aph ^ 1);
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + buf * BN;
+            for (int kb = c0; kb < c1; ++kb, ++it) {
+              const int s = it % STAGES;
+              const uint32_t ph = (it / STAGES) & 1;
+              mbar_wait(full(s), ph);
+              tc_fence_after();
+              const uint32_t a_addr = smem_u32(tiles + s * C::STAGE_BYTES);
+              const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+              for (int kk = 0; kk < BK / 16; ++kk) {  // 32-byte K steps of 8 tf32
+                const uint32_t acc = (kb != c0 || kk != 0) ? 1u : 0u;
+                if constexpr (CG == 2)
+                  umma_tf32_pair(d_tmem, sdesc(a_addr + kk * 32), sdesc(b_addr + kk * 32), C::IDESC_TF, acc);
+                else
+                  umma_tf32(d_tmem, sdesc(a_addr + kk * 32), sdesc(b_addr + kk * 32), C::IDESC_TF, acc);
+              }
+              if constexpr (CG == 2) umma_commit_pair(empty(s));
+              else umma_commit(empty(s));
+            }
+            if constexpr (CG == 2) umma_commit_pair(tfull(buf));
+            else umma_commit(tfull(buf));
+          }
+        }
+      } else {
       for (int i = 0; units.get(i, t, kb0, kb1); ++i, ++tl) {
         const int buf = tl & 1;
         const uint32_t aph = (tl >> 1) & 1;
@@ -298,6 +353,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if constexpr (CG == 2) umma_commit_pair(tfull(buf));
         else umma_commit(tfull(buf));
       }
+      }
     }
   } else {
     // ---------------- epilogue warps 2 .. 2 + EPI_WARPS ----------------
@@ -308,17 +364,64 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t te0 = CG == 2 ? map_rank0(tempty(0)) : tempty(0);
     const uint32_t te1 = CG == 2 ? map_rank0(tempty(1)) : tempty(1);
     int t, kb0, kb1;
+    uint32_t ch = 0;  // TF: accumulation chunks consumed
     for (int i = 0; units.get(i, t, kb0, kb1); ++i, ++tl) {
       const int buf = tl & 1;
       const uint32_t aph = (tl >> 1) & 1;
       int mi_, ni_;
       tile_coords(t, m_tiles, n_tiles, mi_, ni_);
       const int m0 = mi_ * BMT + (int)rank * BM, n0 = ni_ * BN;
-      mbar_wait(tfull(buf), aph);
-      tc_fence_after();
+      uint32_t taddr;
+      if constexpr (TF) {
+        const uint32_t lanes = tmem_base + ((uint32_t)(quad * 32) << 16);
+        // The tensor core adds each MMA's products into its f32 accumulator
+        // with a bias of about 2^-25 of the accumulator per instruction, so a
+        // long K chain drifts (measured 6e-5 relative at K = 5888 through one
+        // accumulator).  Each chunk of TF_CHUNK k-blocks starts a fresh
+        // accumulator; these warps add it into the tile's sum in tensor
+        // memory with round-to-nearest f32 adds (sum buffer 2 + (tl & 1),
+        // this warp's 64 columns) and hand the buffer back at once.
+        const uint32_t sum = lanes + (uint32_t)(2 + (tl & 1)) * BN;
+        for (int c0 = kb0; c0 < kb1; c0 += TF_CHUNK, ++ch) {
+          const int b = ch & 1;
+          mbar_wait(tfull(b), (ch >> 1) & 1);
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 64 * half; c < 64 * half + 64; c += 32) {
+            uint32_t a[32];
+            tmem_ld32(lanes + b * BN, a, c);
+            if (c0 != kb0) {
+              uint32_t sm[32];
+              tmem_ld32(sum, sm, c);
+              tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) a[j] = __float_as_uint(__uint_as_float(a[j]) + __uint_as_float(sm[j]));
+            } else {
+              tmem_wait_ld();
+            }
+            tmem_st32(sum + c, a);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (CG == 2) mbar_arrive_cluster(b ? te1 : te0);
+            else mbar_arrive(tempty(b));
+          }
+        }
+        // the sum's columns come from both warps of each lane quadrant; named
+        // barrier 1 over the epilogue warps (also orders this tile's reads of
+        // the sum before the drains of the tile after next into it)
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * EPI_WARPS) : "memory");
+        tc_fence_after();
+        taddr = sum;
+      } else {
+        mbar_wait(tfull(buf), aph);
+        tc_fence_after();
+        taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * BN;
+      }
       const int row = m0 + quad * 32 + lane;
       const bool row_ok = row < M;
-      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * BN;
       if (ep.mode == EPI_QKVG || ep.mode == EPI_CTXKV) {
 #pragma unroll 1
         for (int c = 128 * half; c < BN; c += 256) {
@@ -451,7 +554,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
+      if (!TF && lane == 0) {
         if constexpr (CG == 2) mbar_arrive_cluster(buf ? te1 : te0);
         else mbar_arrive(tempty(buf));
       }
@@ -466,9 +569,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     if constexpr (CG == 2)
-      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS));
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
     else
-      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS));
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
   }
 }
 
@@ -498,30 +601,34 @@ struct MapKey {
   const void* p;
   long rows, cols, ld;
   int box_rows;
+  bool f32;
   bool operator==(const MapKey& o) const {
-    return p == o.p && rows == o.rows && cols == o.cols && ld == o.ld && box_rows == o.box_rows;
+    return p == o.p && rows == o.rows && cols == o.cols && ld == o.ld && box_rows == o.box_rows && f32 == o.f32;
   }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     return std::hash<const void*>()(k.p) ^ (std::hash<long>()(k.rows) * 31) ^ (std::hash<long>()(k.cols) * 131) ^
-           (std::hash<long>()(k.ld) * 1313) ^ (size_t)k.box_rows;
+           (std::hash<long>()(k.ld) * 1313) ^ (size_t)k.box_rows ^ ((size_t)k.f32 << 20);
   }
 };
 
-const CUtensorMap& tensor_map(const void* p, long rows, long cols, long ld, int box_rows) {
+// Operand map: bf16 {64, box_rows} boxes, or f32 {32, box_rows} (f32 = true);
+// 128-byte rows with the 128-byte swizzle either way.
+const CUtensorMap& tensor_map(const void* p, long rows, long cols, long ld, int box_rows, bool f32 = false) {
   static std::mutex mu;
   static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
   std::lock_guard<std::mutex> lk(mu);
-  MapKey key{p, rows, cols, ld, box_rows};
+  MapKey key{p, rows, cols, ld, box_rows, f32};
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
   CUtensorMap m;
   cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t gstride[1] = {(cuuint64_t)ld * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint64_t gstride[1] = {(cuuint64_t)ld * (f32 ? 4 : 2)};
+  cuuint32_t box[2] = {(cuuint32_t)(f32 ? 32 : BK), (cuuint32_t)box_rows};
   cuuint32_t estride[2] = {1, 1};
-  CUresult r = get_encode()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(p), gdim, gstride, box, estride,
+  CUresult r = get_encode()(&m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                            const_cast<void*>(p), gdim, gstride, box, estride,
                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw Error(IRT_E_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
@@ -576,7 +683,7 @@ int max_pairs() {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int c = 0;
-    if (cudaOccupancyMaxActiveClusters(&c, gemm_kernel<BN, 2>, &cfg) != cudaSuccess || c <= 0) {
+    if (cudaOccupancyMaxActiveClusters(&c, gemm_kernel<BN, 2, false>, &cfg) != cudaSuccess || c <= 0) {
       cudaGetLastError();
       c = num_sms() / 2;
     }
@@ -585,19 +692,22 @@ int max_pairs() {
   return n;
 }
 
-template <int BN, int CG>
-void launch(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int K, int splits, const EpiParams& p,
+// TF: A and B are [A_hi | A_lo] / [B_hi | B_lo] f32 matrices of 2K columns.
+template <int BN, int CG, bool TF>
+void launch(const void* A, long lda, const void* B, long ldb, int M, int N, int K, int splits, const EpiParams& p,
             cudaStream_t s) {
   using C = Cfg<BN, CG>;
   static unsigned attr_mask = 0;  // per-device opt-in to the large dynamic smem
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_mask & (1u << (dev & 31)))) {
-    IRT_CUDA(cudaFuncSetAttribute(gemm_kernel<BN, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
+    IRT_CUDA(
+        cudaFuncSetAttribute(gemm_kernel<BN, CG, TF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
     attr_mask |= 1u << (dev & 31);
   }
-  const CUtensorMap ta = tensor_map(A, M, K, lda, BM);  // copies: the cache may be cleared
-  const CUtensorMap tb = tensor_map(B, N, K, ldb, C::B_ROWS);
+  const long cols = TF ? 2L * K : K;
+  const CUtensorMap ta = tensor_map(A, M, cols, lda, BM, TF);  // copies: the cache may be cleared
+  const CUtensorMap tb = tensor_map(B, N, cols, ldb, C::B_ROWS, TF);
   // residual by TMA reduce-add (not for row-masked residuals)
   const bool xtma = p.mode == EPI_RESID && !p.row_scale && p.x && (N % 32) == 0 &&
                     (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 &&
@@ -609,7 +719,7 @@ void launch(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int 
   const int units = splits < 0 ? (1 << 30) : ((M + BM * CG - 1) / (BM * CG)) * ((N + BN - 1) / BN) * splits;
   if constexpr (CG == 1) {
     const int grid = units < num_sms() ? units : num_sms();
-    launch_pdl(gemm_kernel<BN, 1>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, tx, M, N, K, splits, pp);
+    launch_pdl(gemm_kernel<BN, 1, TF>, dim3(grid), dim3(THREADS), C::SMEM, s, ta, tb, tx, M, N, K, splits, pp);
   } else {
     const int pairs = std::min(units, max_pairs<BN>());
     cudaLaunchConfig_t cfg = {};
@@ -626,7 +736,7 @@ void launch(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
-    IRT_CUDA(cudaLaunchKernelEx(&cfg, gemm_kernel<BN, 2>, ta, tb, tx, M, N, K, splits, pp));
+    IRT_CUDA(cudaLaunchKernelEx(&cfg, gemm_kernel<BN, 2, TF>, ta, tb, tx, M, N, K, splits, pp));
   }
   IRT_CHECK_LAUNCH();
 }
@@ -716,8 +826,10 @@ bool gemm_tc_supported(const EpiParams& p, int K, long lda, long ldb, const void
   return true;
 }
 
-void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int K, const EpiParams& p,
-             cudaStream_t s) {
+namespace tc {
+template <bool TF>
+void gemm_tc_impl(const void* A, long lda, const void* B, long ldb, int M, int N, int K, const EpiParams& p,
+                  cudaStream_t s) {
   // Tile width 256 wherever the epilogue allows it.  Narrower tiles fill the
   // last wave better at small M but re-read A from L2 twice as often, and
   // measured slower at every M tried (750-54,504 rows).
@@ -727,7 +839,7 @@ void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int
   const int bmt = pairs ? 2 * tc::BM : tc::BM;
   const long mt = (M + bmt - 1) / bmt;
   const long t256 = mt * ((N + 255) / 256), t128 = mt * ((N + 127) / 128);
-  bool use256 = N >= 256;
+  bool use256 = N >= 256 && !TF;  // TF: 128-column tiles (the tile sums need the TMEM)
   if ((p.mode == EPI_QKVG || p.mode == EPI_CTXKV) && (p.Dq % 256)) use256 = false;
   // K-splits for the additive residual epilogue (partial products are
   // reduce-added into x): the split count that best fills the last wave of
@@ -740,7 +852,7 @@ void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int
   // W2 at 3,400 rows and slower than the split rule wherever that one splits.
   int splits = 1;
   const long tiles = use256 ? t256 : t128;
-  if (p.mode == EPI_RESID && !p.row_scale) {
+  if (!TF && p.mode == EPI_RESID && !p.row_scale) {
     const int kb = (K + tc::BK - 1) / tc::BK;
     const double eff1 = tc::wave_eff(tiles, sms);
     double best = eff1;
@@ -763,13 +875,70 @@ void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int
                          (!p.gate || (reinterpret_cast<uintptr_t>(p.gate) & 15) == 0);
     if (splits == 1 && xtma_ok && !ts_off && tc::tail_split_pays(tiles, sms, kb, ts_force)) splits = -2;
   }
-  if (pairs) {
-    if (use256) tc::launch<256, 2>(A, lda, B, ldb, M, N, K, splits, p, s);
-    else tc::launch<128, 2>(A, lda, B, ldb, M, N, K, splits, p, s);
+  if constexpr (TF) {
+    if (pairs) tc::launch<128, 2, true>(A, lda, B, ldb, M, N, K, splits, p, s);
+    else tc::launch<128, 1, true>(A, lda, B, ldb, M, N, K, splits, p, s);
+  } else if (pairs) {
+    if (use256) tc::launch<256, 2, false>(A, lda, B, ldb, M, N, K, splits, p, s);
+    else tc::launch<128, 2, false>(A, lda, B, ldb, M, N, K, splits, p, s);
   } else {
-    if (use256) tc::launch<256, 1>(A, lda, B, ldb, M, N, K, splits, p, s);
-    else tc::launch<128, 1>(A, lda, B, ldb, M, N, K, splits, p, s);
+    if (use256) tc::launch<256, 1, false>(A, lda, B, ldb, M, N, K, splits, p, s);
+    else tc::launch<128, 1, false>(A, lda, B, ldb, M, N, K, splits, p, s);
   }
+}
+
+// hi = a rounded to the nearest tf32 (ties away from zero; the 13 low mantissa
+// bits cleared), lo = a - hi (exact in f32).  Inf / NaN pass through as hi.
+__device__ __forceinline__ float tf32_hi(float a) {
+  const uint32_t u = __float_as_uint(a);
+  if ((u & 0x7f800000u) == 0x7f800000u) return a;
+  return __uint_as_float((u + 0x1000u) & 0xffffe000u);
+}
+
+// Row m of A [M, K] (leading dimension lda) -> row m of A2 = [A_hi | A_lo]
+// [M, 2 * Kp], columns K..Kp-1 of each half zero.  Four columns per thread.
+__global__ void split_tf32_kernel(const float* __restrict__ A, long lda, int M, int K, float* __restrict__ A2,
+                                  int Kp) {
+  pdl_wait();
+  pdl_trigger();
+  const int q = Kp / 4;
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)M * q) return;
+  const int m = (int)(i / q), k = (int)(i - (long)m * q) * 4;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (k + 3 < K) {
+    a = *reinterpret_cast<const float4*>(A + (long)m * lda + k);
+  } else {
+    const float* r = A + (long)m * lda;
+    if (k < K) a.x = r[k];
+    if (k + 1 < K) a.y = r[k + 1];
+    if (k + 2 < K) a.z = r[k + 2];
+  }
+  const float4 h = make_float4(tf32_hi(a.x), tf32_hi(a.y), tf32_hi(a.z), tf32_hi(a.w));
+  float* o = A2 + (long)m * 2 * Kp + k;
+  *reinterpret_cast<float4*>(o) = h;
+  *reinterpret_cast<float4*>(o + Kp) = make_float4(a.x - h.x, a.y - h.y, a.z - h.z, a.w - h.w);
+}
+}  // namespace tc
+
+void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int K, const EpiParams& p,
+             cudaStream_t s) {
+  tc::gemm_tc_impl<false>(A, lda, B, ldb, M, N, K, p, s);
+}
+
+void gemm_tc_tf32x3(const float* A2, long lda2, const float* B2, long ldb2, int M, int N, int Kp, const EpiParams& p,
+                    cudaStream_t s) {
+  if (Kp % 32) throw Error(IRT_E_INVALID_ARG, "gemm_tc_tf32x3: K must be padded to a multiple of 32");
+  tc::gemm_tc_impl<true>(A2, lda2, B2, ldb2, M, N, Kp, p, s);
+}
+
+void split_tf32(const float* A, long lda, int M, int K, float* A2, int Kp, cudaStream_t s) {
+  if (M <= 0) return;
+  if (Kp % 32 || Kp < K || (lda % 4) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(A2) & 15))
+    throw Error(IRT_E_INVALID_ARG, "split_tf32: unaligned operand");
+  const long n = (long)M * (Kp / 4);
+  launch_pdl(tc::split_tf32_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, A, lda, M, K, A2, Kp);
+  IRT_CHECK_LAUNCH();
 }
 
 }  // namespace irt

@@ -77,6 +77,15 @@ void epilogue_apply(const EpiParams& p, const float* raw, long ldr, long r_bstri
 bool gemm_tc_supported(const EpiParams& p, int K, long lda, long ldb, const void* A, const void* B);
 void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int K, const EpiParams& p,
              cudaStream_t s);
+// f32 GEMM on the tcgen05 tf32 path with the same epilogues: A2 = [A_hi | A_lo]
+// [M, 2 Kp] and B2 = [B_hi | B_lo] [N, 2 Kp] from split_tf32 (Kp = K rounded
+// up to a multiple of 32, zero columns in between); C = A_hi.B_hi + A_hi.B_lo +
+// A_lo.B_hi accumulated in f32.  Shape checks as gemm_tc_supported with K = Kp.
+void gemm_tc_tf32x3(const float* A2, long lda2, const float* B2, long ldb2, int M, int N, int Kp, const EpiParams& p,
+                    cudaStream_t s);
+// A [M, K] f32 (lda % 4 == 0, 16-byte aligned) -> A2 [M, 2 Kp] as above.
+void split_tf32(const float* A, long lda, int M, int K, float* A2, int Kp, cudaStream_t s);
+inline int tf32_kpad(int K) { return (K + 31) / 32 * 32; }
 // Device-side watchdog flag of the GEMM kernels (0 = ok).
 int read_and_clear_kernel_error();
 // Watchdog probes (test hooks): run tcx::watchdog_probe_kernel in the GEMM /

@@ -64,6 +64,43 @@ IRTT_API int irtt_gemm_simt(const void* A, int a_bf16, long lda, long a_bs, cons
   });
 }
 
+// f32 GEMM as the f32 engine runs it: path 0 = the tcgen05 tf32 hi / lo split
+// product (both operands split here), 1 = SIMT + epilogue.  mode EPI_STORE
+// (out = C [M, N] f32) or EPI_RESID (out = x [M, N] += gate . acc).
+IRTT_API int irtt_gemm_f32(int mode, const float* A, const float* B, int M, int N, int K, int path, float* out,
+                           const float* gate) {
+  return guard([&] {
+    irt::EpiParams p;
+    p.mode = mode;
+    p.M = M;
+    p.N = N;
+    p.out_bf16 = 0;
+    if (mode == irt::EPI_RESID) {
+      p.x = out;
+      p.gate = gate;
+    } else {
+      p.out = out;
+      p.ldo = N;
+    }
+    if (path == 0) {
+      const int Kp = irt::tf32_kpad(K);
+      irt::DevBuf a2((size_t)M * 2 * Kp * 4), b2((size_t)N * 2 * Kp * 4);
+      if (!irt::gemm_tc_supported(p, Kp, 2L * Kp, 2L * Kp, a2.p, b2.p))
+        throw irt::Error(4, "shape not supported by tcgen05 path");
+      irt::split_tf32(A, K, M, K, a2.as<float>(), Kp, nullptr);
+      irt::split_tf32(B, K, N, K, b2.as<float>(), Kp, nullptr);
+      irt::gemm_tc_tf32x3(a2.as<float>(), 2L * Kp, b2.as<float>(), 2L * Kp, M, N, Kp, p, nullptr);
+      IRT_CUDA(cudaDeviceSynchronize());
+      if (irt::read_and_clear_kernel_error()) throw irt::Error(20, "GEMM watchdog fired");
+    } else {
+      irt::DevBuf raw((size_t)M * N * 4);
+      irt::gemm_simt(A, 0, K, 0, B, 0, K, 0, raw.as<float>(), N, 0, M, N, K, 1, nullptr);
+      irt::epilogue_apply(p, raw.as<float>(), N, 0, 1, nullptr);
+      IRT_CUDA(cudaDeviceSynchronize());
+    }
+  });
+}
+
 // Fused-epilogue GEMM for the QKVG / SWIGLU / RESID modes with bf16 operands.
 IRTT_API int irtt_gemm_epi(int mode, const void* A, const void* B, int M, int N, int K, int path, void* o0, void* o1,
                            void* o2, void* o3, const float* w0, const float* w1, const float* cos_t,

@@ -346,6 +346,46 @@ def test_attention_key_mask_and_empty_rows(dev, bf16, path):
     assert err < (2e-2 if bf16 else 1e-5), f"rel err {err}"
 
 
+F32_GEMM_CASES = [
+    (256, 256, 64, 0),     # smallest pair tile, one k-block per segment
+    (300, 384, 100, 0),    # K padded to 128 (zero columns between the hi and lo halves), partial n-tile
+    (130, 2048, 1280, 0),  # single-CTA tiles (fewer than 256 rows)
+    (750, 8192, 2048, 0),  # QKV+gate width at config-1 rows
+    (750, 2048, 5888, 2),  # W2 residual at config-1 rows (K-splits across the three segments)
+    (1500, 2048, 2048, 2),  # Wo residual
+    (3400, 2048, 5888, 2),  # W2 residual at ~3,400 rows (stream-K / tail split)
+]
+
+
+@pytest.mark.parametrize("M,N,K,mode", F32_GEMM_CASES)
+@pytest.mark.parametrize("path", [0, 1])
+def test_gemm_f32_split_tf32_matches_f64(dev, M, N, K, mode, path):
+    """The f32 mode's GEMM: path 0 = tcgen05 tf32 with hi / lo operand halves
+    (A_hi.B_hi + A_hi.B_lo + A_lo.B_hi), path 1 = SIMT f32, both against an f64
+    product.  The bound (1e-5 of the largest output) holds for f32 arithmetic
+    and fails for a single tf32 product (~1e-4 at these sizes)."""
+    if path == 1 and M * N * K > 4e9:
+        pytest.skip("SIMT path checked on the smaller shapes")
+    L = hooks()
+    L.irtt_gemm_f32.argtypes = [ctypes.c_int] + [ctypes.c_void_p] * 2 + [ctypes.c_int] * 4 + [ctypes.c_void_p] * 2
+    g = torch.Generator(device=dev).manual_seed(M + 3 * N + 7 * K + mode)
+    A = torch.randn(M, K, device=dev, generator=g)
+    B = torch.randn(N, K, device=dev, generator=g) * 0.05
+    prod = A.double() @ B.double().T
+    if mode == 2:
+        x = torch.randn(M, N, device=dev, generator=g)
+        gate = torch.randn(N, device=dev, generator=g)
+        ref = x.double() + gate.double() * prod
+        check(L.irtt_gemm_f32(mode, ptr(A), ptr(B), M, N, K, path, ptr(x), ptr(gate)))
+        out = x
+    else:
+        ref = prod
+        out = torch.full((M, N), float("nan"), device=dev)
+        check(L.irtt_gemm_f32(mode, ptr(A), ptr(B), M, N, K, path, ptr(out), None))
+    err = (out.double() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-5, f"f32 GEMM rel max err {err}"
+
+
 @pytest.mark.parametrize("force", ["1", None])
 @pytest.mark.parametrize("M,K", [(54504, 2048), (27252, 5888), (6800, 5888), (1000, 1024)])
 def test_gemm_resid_tail_split(dev, monkeypatch, force, M, K):
