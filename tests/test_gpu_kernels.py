@@ -363,7 +363,8 @@ def test_gemm_f32_split_tf32_matches_f64(dev, M, N, K, mode, path):
     """The f32 mode's GEMM: path 0 = tcgen05 tf32 with hi / lo operand halves
     (A_hi.B_hi + A_hi.B_lo + A_lo.B_hi), path 1 = SIMT f32, both against an f64
     product.  The bound (1e-5 of the largest output) holds for f32 arithmetic
-    and fails for a single tf32 product (~1e-4 at these sizes)."""
+    and fails for a single tf32 product (~1e-4 at these sizes); path 0's
+    relative L2 error must also stay below 1 % of cuBLAS's TF32 product's."""
     if path == 1 and M * N * K > 4e9:
         pytest.skip("SIMT path checked on the smaller shapes")
     L = hooks()
@@ -383,6 +384,21 @@ def test_gemm_f32_split_tf32_matches_f64(dev, M, N, K, mode, path):
         out = torch.full((M, N), float("nan"), device=dev)
         check(L.irtt_gemm_f32(mode, ptr(A), ptr(B), M, N, K, path, ptr(out), None))
     err = (out.double() - ref).abs().max().item() / ref.abs().max().item()
+    l2 = ((out.double() - ref).norm() / ref.norm()).item()
+    ctx = ""
+    if path == 0 and mode == 0:  # the same product through cuBLAS with TF32 off and on, for scale
+        prev = torch.backends.cuda.matmul.allow_tf32
+        try:
+            l2s = {}
+            for tf in (False, True):
+                torch.backends.cuda.matmul.allow_tf32 = tf
+                c = (A @ B.T).double()
+                l2s[tf] = ((c - prod).norm() / prod.norm()).item()
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = prev
+        ctx = f"; cuBLAS f32 {l2s[False]:.2e}, cuBLAS tf32 {l2s[True]:.2e}"
+        assert l2 < 0.01 * l2s[True], (l2, l2s)
+    print(f"f32 GEMM path {path} M={M} N={N} K={K} mode={mode}: rel-L2 {l2:.2e}, rel max {err:.2e}{ctx}")
     assert err < 1e-5, f"f32 GEMM rel max err {err}"
 
 
