@@ -272,6 +272,8 @@ Codec::Codec(int dev, const std::string& path, int precision) : device(dev), pre
   IRT_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   SafeTensorsFile st(path);
   auto get = [&](const std::string& k, size_t rank) -> const TensorView& { return st.get(k, rank); };
+  const char* simt = std::getenv("IRT_CODEC_F32_SIMT");
+  const bool want_tf32 = prec == IRT_PREC_F32 && !(simt && simt[0] == '1');
   // 1 / (alpha + 1e-9) in f32, the Snake epilogue's reciprocal (a correctly
   // rounded divide, as the kernels would compute it)
   auto add_inv = [&](const DevBuf& alpha, const std::vector<float>& h) {
@@ -289,6 +291,7 @@ Codec::Codec(int dev, const std::string& path, int precision) : device(dev), pre
     c.pad = (c.k - 1) * dil / 2;  // conv_pad(k, 1, dil) (src/codec/layers.rs:64-66)
     up_host(c.w, h);
     if (st.has(p + ".bias")) up_f32(c.b, get(p + ".bias", 1));
+    if (want_tf32 && c.cout > 1) codec_pack_tf32_conv(c, h);
     if (prec == IRT_PREC_BF16 && c.cout % 32 == 0 && c.cin % 8 == 0) {
       c.cin_pad = round_up64(c.cin);
       up_bf16(c.wp, pack_conv(h, c.cout, c.cin, c.k, c.cin_pad));
@@ -311,6 +314,7 @@ Codec::Codec(int dev, const std::string& path, int precision) : device(dev), pre
     bl.ct.pad = (bl.stride + 1) / 2;  // conv_transpose_pad (src/codec/layers.rs:71-75)
     up_host(bl.ct.w, h);
     if (st.has(p + ".block.1.bias")) up_f32(bl.ct.b, get(p + ".block.1.bias", 1));
+    if (want_tf32) codec_pack_tf32_convt(bl.ct, h, bl.stride);
     if (prec == IRT_PREC_BF16 && bl.ct.cout % 32 == 0 && bl.ct.cin % 8 == 0 && bl.stride >= 2) {
       bl.ct.cin_pad = round_up64(bl.ct.cin);
       bl.ct.phases = bl.stride;
@@ -340,6 +344,7 @@ Codec::Codec(int dev, const std::string& path, int precision) : device(dev), pre
     }
     tc = ok;
   }
+  tf32 = want_tf32 && codec_tf32_supported(*this);
   codec_noalloc_prepare();
 }
 
@@ -436,6 +441,10 @@ void Codec::decode(const float* latent, int B, int T, float* wav, int memory, cu
   if (ragged) IRT_CUDA(cudaMemsetAsync(out, 0, wav_bytes, s));
   if (tc) {
     decode_tc(in.as<float>(), B, T, ragged ? lengths : nullptr, out, s);
+  } else if (tf32) {
+    for (int b = 0; b < B; ++b)  // each utterance at its own length
+      codec_decode_tf32(*this, in.as<float>() + (size_t)b * T * 32, ragged ? lengths[b] : T,
+                        out + (size_t)b * T * hop, s);
   } else if (!ragged) {
     decode_simt(*this, in.as<float>(), B, T, out, s);
   } else {
@@ -447,6 +456,8 @@ void Codec::decode(const float* latent, int B, int T, float* wav, int memory, cu
   IRT_CUDA(cudaStreamSynchronize(s));
   if (tc && conv_tc_read_and_clear_error())
     throw Error(IRT_E_CUDA, "codec tensor-core kernel watchdog expired (pipeline stalled)");
+  if (tf32 && read_and_clear_kernel_error())
+    throw Error(IRT_E_CUDA, "codec tf32 GEMM watchdog expired (pipeline stalled)");
   last_launches = launch_counter().load() - l0;
 }
 

@@ -44,6 +44,9 @@ struct Codec {
     DevBuf w, b;
     DevBuf wp;  // bf16 mode: packed [phases][cout][taps][cin_pad]
     int cin_pad = 0, phases = 1;
+    // f32 mode on the tf32 GEMM: per phase [cout_pad][hi: taps x cp | lo: taps x cp]
+    DevBuf w2;
+    int cp = 0, cout_pad = 0;
   };
   struct Res {
     DevBuf a0, a2;
@@ -69,6 +72,10 @@ struct Codec {
   // bf16 tensor-core path: row buffers and the frame table
   bool tc = false;
   DevBuf rx, rp, rq, frames, wav_dev;
+  // f32 mode: every convolution on the tf32 hi / lo GEMM (codec_tf32.cu),
+  // unless IRT_CODEC_F32_SIMT=1 or a layer does not fit it (then SIMT)
+  bool tf32 = false;
+  DevBuf fx, fy, fa2, fmap;
   long long last_launches = 0;
 
   Codec(int dev, const std::string& path, int precision);
@@ -82,6 +89,13 @@ struct Codec {
   void pack_tc_weights();
   void decode_tc(const float* latent_dev, int B, int T, const int* lengths, float* wav_dev, cudaStream_t s);
 };
+
+// f32 decode on the tf32 GEMM (codec_tf32.cu): weight packing at load, the
+// support check, and the decode of one utterance (lat [T, 32], wav [T * hop]).
+void codec_pack_tf32_conv(Codec::Conv& c, const std::vector<float>& w);
+void codec_pack_tf32_convt(Codec::Conv& c, const std::vector<float>& w, int stride);
+bool codec_tf32_supported(const Codec& c);
+void codec_decode_tf32(Codec& c, const float* lat, int T, float* wav, cudaStream_t s);
 
 // Allocation-free decode into a fixed device scratch array (codec_noalloc.cu).
 void codec_decode_noalloc(Codec& c, const float* latent, int B, int T, float* wav, cudaStream_t s);

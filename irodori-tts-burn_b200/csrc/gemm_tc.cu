@@ -41,10 +41,20 @@ namespace tc {
 constexpr int BM = 128, BK = 64, EPI_WARPS = 8, THREADS = 64 + 32 * EPI_WARPS;
 // Smallest k-block span of a group in a tail split (splits == -2).
 constexpr int TAIL_MIN_SPAN = 8;
-// TF: k-blocks per accumulator chunk (each chunk's MMA chain restarts at 0
-// and is added into the tile sum by the epilogue warps).
-constexpr int TF_CHUNK = 8;
+// TF: k-blocks per accumulator chunk in the A_hi.B_hi segment (each chunk's
+// MMA chain restarts at 0 and is added into the tile sum by the epilogue
+// warps); the two small-term segments (A_hi.B_lo, A_lo.B_hi, ~2^-11 of the
+// product) run one chunk each, so a chunk never adds small terms onto a large
+// accumulator.
+constexpr int TF_CHUNK = 2;
 constexpr uint32_t A_BYTES = BM * BK * 2;
+
+// End of the TF accumulation chunk that starts at k-block c0 (segments of
+// kseg k-blocks; the unit ends at kb1).
+__device__ __forceinline__ int tf_chunk_end(int c0, int kb1, int kseg) {
+  const int seg_end = (c0 / kseg + 1) * kseg;
+  return min(kb1, c0 < kseg ? min(seg_end, c0 + TF_CHUNK) : seg_end);
+}
 
 // CG = CTAs per MMA: 1, or 2 for a CTA pair (cluster of 2) that computes a
 // 256-row tile with tcgen05.mma.cta_group::2.  In a pair each CTA stages its
@@ -263,22 +273,27 @@ __global__ void __launch_bounds__(THREADS, 1)
           mbar_wait(empty(s), ph ^ 1);
           uint8_t* a_dst = tiles + s * C::STAGE_BYTES;
           uint8_t* b_dst = a_dst + A_BYTES;
-          int ca = kb * BK, cb = kb * BK;  // element columns of the A and B boxes
+          int ca = kb * BK, cb = kb * BK, ra = m0;  // columns of the A and B boxes, A's first row
           if constexpr (TF) {
-            const int kseg = K / 32, seg = kb / kseg, kk = (kb - seg * kseg) * 32;
-            ca = (seg == 2 ? K : 0) + kk;
-            cb = (seg == 1 ? K : 0) + kk;
+            // K = taps x Cin_p per segment; A2 = [hi | lo] is [rows, 2 Cin_p] and
+            // tap j reads A rows shifted by j * conv_dil - conv_pad (implicit
+            // convolution; plain GEMM: one tap, no shift)
+            const int kseg = K / 32, seg = kb / kseg, kk = kb - seg * kseg;
+            const int cblocks = kseg / ep.conv_taps, tap = kk / cblocks, cblk = kk - tap * cblocks;
+            ca = (seg == 2 ? cblocks * 32 : 0) + cblk * 32;
+            cb = (seg == 1 ? K : 0) + kk * 32;
+            ra = m0 + tap * ep.conv_dil - ep.conv_pad;
           }
           if constexpr (CG == 2) {
             // both CTAs' copies complete on rank 0's full barrier, which
             // expects the pair's bytes
             const uint32_t fb = map_rank0(full(s));
             if (rank == 0) mbar_expect_tx(full(s), CG * C::STAGE_BYTES);
-            tma_load_2d_pair(smem_u32(a_dst), &tmA, fb, ca, m0);
+            tma_load_2d_pair(smem_u32(a_dst), &tmA, fb, ca, ra);
             tma_load_2d_pair(smem_u32(b_dst), &tmB, fb, cb, n0);
           } else {
             mbar_expect_tx(full(s), C::STAGE_BYTES);
-            tma_load_2d(smem_u32(a_dst), &tmA, full(s), ca, m0);
+            tma_load_2d(smem_u32(a_dst), &tmA, full(s), ca, ra);
             tma_load_2d(smem_u32(b_dst), &tmB, full(s), cb, n0);
           }
         }
@@ -290,11 +305,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t it = 0, tl = 0;
       int t, kb0, kb1;
       if constexpr (TF) {
-        // accumulation chunks of TF_CHUNK k-blocks, alternating between the
-        // two accumulator buffers (tl counts chunks here)
+        // accumulation chunks (tf_chunk_end), alternating between the two
+        // accumulator buffers (tl counts chunks here)
         for (int i = 0; units.get(i, t, kb0, kb1); ++i) {
-          for (int c0 = kb0; c0 < kb1; c0 += TF_CHUNK, ++tl) {
-            const int c1 = min(kb1, c0 + TF_CHUNK);
+          for (int c0 = kb0, c1; c0 < kb1; c0 = c1, ++tl) {
+            c1 = tf_chunk_end(c0, kb1, K / 32);
             const int buf = tl & 1;
             const uint32_t aph = (tl >> 1) & 1;
             mbar_wait(tempty(buf), aph ^ 1);
@@ -374,44 +389,58 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t taddr;
       if constexpr (TF) {
         const uint32_t lanes = tmem_base + ((uint32_t)(quad * 32) << 16);
-        // The tensor core adds each MMA's products into its f32 accumulator
-        // with a bias of about 2^-25 of the accumulator per instruction, so a
-        // long K chain drifts (measured 6e-5 relative at K = 5888 through one
-        // accumulator).  Each chunk of TF_CHUNK k-blocks starts a fresh
-        // accumulator; these warps add it into the tile's sum in tensor
-        // memory with round-to-nearest f32 adds (sum buffer 2 + (tl & 1),
-        // this warp's 64 columns) and hand the buffer back at once.
+        // The tensor core's f32 accumulation loses accuracy with every MMA
+        // chained into one accumulator (measured relative L2 against f64: 6e-5
+        // at K = 5888 in one chain; 6.5e-7 with 8-k-block chunks; 2e-7 to
+        // 4.4e-7 with 2-k-block chunks).  Each chunk (tf_chunk_end) starts a
+        // fresh accumulator; these warps read it (this warp's 64 columns),
+        // hand the buffer back at once and add it into the tile sum in their
+        // registers with round-to-nearest f32 adds; the sum goes to tensor
+        // memory (sum buffer 2 + (tl & 1)) for the epilogue below.
         const uint32_t sum = lanes + (uint32_t)(2 + (tl & 1)) * BN;
-        for (int c0 = kb0; c0 < kb1; c0 += TF_CHUNK, ++ch) {
+        float acc[64];  // this thread's row, this warp's 64 columns of the tile sum
+        auto take = [&](bool first) {  // one chunk: into acc, then the buffer goes back
           const int b = ch & 1;
           mbar_wait(tfull(b), (ch >> 1) & 1);
           tc_fence_after();
-#pragma unroll 1
-          for (int c = 64 * half; c < 64 * half + 64; c += 32) {
-            uint32_t a[32];
-            tmem_ld32(lanes + b * BN, a, c);
-            if (c0 != kb0) {
-              uint32_t sm[32];
-              tmem_ld32(sum, sm, c);
-              tmem_wait_ld();
+          uint32_t a[32];
+          tmem_ld32(lanes + b * BN, a, 64 * half);
+          tmem_wait_ld();
 #pragma unroll
-              for (int j = 0; j < 32; ++j) a[j] = __float_as_uint(__uint_as_float(a[j]) + __uint_as_float(sm[j]));
-            } else {
-              tmem_wait_ld();
-            }
-            tmem_st32(sum + c, a);
-          }
-          tmem_wait_st();
+          for (int j = 0; j < 32; ++j) acc[j] = first ? __uint_as_float(a[j]) : acc[j] + __uint_as_float(a[j]);
+          tmem_ld32(lanes + b * BN, a, 64 * half + 32);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            acc[32 + j] = first ? __uint_as_float(a[j]) : acc[32 + j] + __uint_as_float(a[j]);
           tc_fence_before();
           __syncwarp();
           if (lane == 0) {
             if constexpr (CG == 2) mbar_arrive_cluster(b ? te1 : te0);
             else mbar_arrive(tempty(b));
           }
+          ++ch;
+        };
+        int c1 = tf_chunk_end(kb0, kb1, K / 32);
+        take(true);
+        for (int c0 = c1; c0 < kb1; c0 = c1) {
+          c1 = tf_chunk_end(c0, kb1, K / 32);
+          take(false);
+        }
+        {
+          uint32_t o[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(acc[j]);
+          tmem_st32(sum + 64 * half, o);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(acc[32 + j]);
+          tmem_st32(sum + 64 * half + 32, o);
+          tmem_wait_st();
+          tc_fence_before();
         }
         // the sum's columns come from both warps of each lane quadrant; named
         // barrier 1 over the epilogue warps (also orders this tile's reads of
-        // the sum before the drains of the tile after next into it)
+        // the sum before the store of the tile after next into it)
         asm volatile("bar.sync 1, %0;" ::"n"(32 * EPI_WARPS) : "memory");
         tc_fence_after();
         taddr = sum;
@@ -692,10 +721,13 @@ int max_pairs() {
   return n;
 }
 
-// TF: A and B are [A_hi | A_lo] / [B_hi | B_lo] f32 matrices of 2K columns.
+// TF: A and B are [A_hi | A_lo] / [B_hi | B_lo] f32 matrices of 2 K / taps and
+// 2 K columns.  a_rows / b_rows > 0: the rows their tensor maps span (the
+// rows that exist, zero padding included, so that no box is taller than its
+// tensor; rows past them read as zero), else M / N.
 template <int BN, int CG, bool TF>
 void launch(const void* A, long lda, const void* B, long ldb, int M, int N, int K, int splits, const EpiParams& p,
-            cudaStream_t s) {
+            cudaStream_t s, long a_rows = 0, long b_rows = 0) {
   using C = Cfg<BN, CG>;
   static unsigned attr_mask = 0;  // per-device opt-in to the large dynamic smem
   int dev = 0;
@@ -705,9 +737,10 @@ void launch(const void* A, long lda, const void* B, long ldb, int M, int N, int 
         cudaFuncSetAttribute(gemm_kernel<BN, CG, TF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
     attr_mask |= 1u << (dev & 31);
   }
-  const long cols = TF ? 2L * K : K;
-  const CUtensorMap ta = tensor_map(A, M, cols, lda, BM, TF);  // copies: the cache may be cleared
-  const CUtensorMap tb = tensor_map(B, N, cols, ldb, C::B_ROWS, TF);
+  const long acols = TF ? 2L * (K / p.conv_taps) : K, bcols = TF ? 2L * K : K;
+  // copies: the cache may be cleared
+  const CUtensorMap ta = tensor_map(A, a_rows > 0 ? a_rows : M, acols, lda, BM, TF);
+  const CUtensorMap tb = tensor_map(B, b_rows > 0 ? b_rows : N, bcols, ldb, C::B_ROWS, TF);
   // residual by TMA reduce-add (not for row-masked residuals)
   const bool xtma = p.mode == EPI_RESID && !p.row_scale && p.x && (N % 32) == 0 &&
                     (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 &&
@@ -829,7 +862,7 @@ bool gemm_tc_supported(const EpiParams& p, int K, long lda, long ldb, const void
 namespace tc {
 template <bool TF>
 void gemm_tc_impl(const void* A, long lda, const void* B, long ldb, int M, int N, int K, const EpiParams& p,
-                  cudaStream_t s) {
+                  cudaStream_t s, long a_rows = 0, long b_rows = 0) {
   // Tile width 256 wherever the epilogue allows it.  Narrower tiles fill the
   // last wave better at small M but re-read A from L2 twice as often, and
   // measured slower at every M tried (750-54,504 rows).
@@ -876,8 +909,8 @@ void gemm_tc_impl(const void* A, long lda, const void* B, long ldb, int M, int N
     if (splits == 1 && xtma_ok && !ts_off && tc::tail_split_pays(tiles, sms, kb, ts_force)) splits = -2;
   }
   if constexpr (TF) {
-    if (pairs) tc::launch<128, 2, true>(A, lda, B, ldb, M, N, K, splits, p, s);
-    else tc::launch<128, 1, true>(A, lda, B, ldb, M, N, K, splits, p, s);
+    if (pairs) tc::launch<128, 2, true>(A, lda, B, ldb, M, N, K, splits, p, s, a_rows, b_rows);
+    else tc::launch<128, 1, true>(A, lda, B, ldb, M, N, K, splits, p, s, a_rows, b_rows);
   } else if (pairs) {
     if (use256) tc::launch<256, 2, false>(A, lda, B, ldb, M, N, K, splits, p, s);
     else tc::launch<128, 2, false>(A, lda, B, ldb, M, N, K, splits, p, s);
@@ -927,9 +960,10 @@ void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int
 }
 
 void gemm_tc_tf32x3(const float* A2, long lda2, const float* B2, long ldb2, int M, int N, int Kp, const EpiParams& p,
-                    cudaStream_t s) {
-  if (Kp % 32) throw Error(IRT_E_INVALID_ARG, "gemm_tc_tf32x3: K must be padded to a multiple of 32");
-  tc::gemm_tc_impl<true>(A2, lda2, B2, ldb2, M, N, Kp, p, s);
+                    cudaStream_t s, long a_rows, long b_rows) {
+  if (Kp % 32 || p.conv_taps < 1 || (Kp / 32) % p.conv_taps)
+    throw Error(IRT_E_INVALID_ARG, "gemm_tc_tf32x3: K must be taps x a multiple of 32");
+  tc::gemm_tc_impl<true>(A2, lda2, B2, ldb2, M, N, Kp, p, s, a_rows, b_rows);
 }
 
 void split_tf32(const float* A, long lda, int M, int K, float* A2, int Kp, cudaStream_t s) {

@@ -62,6 +62,10 @@ struct EpiParams {
   int Dq = 0;
   // batched launches (SIMT path only): per-z offsets
   long bias_bstride = 0, out_bstride = 0, add_bstride = 0;
+  // gemm_tc_tf32x3 as an implicit convolution: K = conv_taps x Cin_p and tap
+  // j of output row m reads A row m + j * conv_dil - conv_pad (rows outside
+  // [0, rows of A) read as zero)
+  int conv_taps = 1, conv_dil = 1, conv_pad = 0;
 };
 
 // fp32 SIMT GEMM into a raw accumulator buffer, then the epilogue kernel.
@@ -81,8 +85,11 @@ void gemm_tc(const bf16* A, long lda, const bf16* B, long ldb, int M, int N, int
 // [M, 2 Kp] and B2 = [B_hi | B_lo] [N, 2 Kp] from split_tf32 (Kp = K rounded
 // up to a multiple of 32, zero columns in between); C = A_hi.B_hi + A_hi.B_lo +
 // A_lo.B_hi accumulated in f32.  Shape checks as gemm_tc_supported with K = Kp.
+// a_rows / b_rows > 0: the rows of A2 / B2 that exist (zero padding included,
+// at least one 128-row box); the tensor maps span exactly those and rows past
+// them read as zero.  0: M / N.
 void gemm_tc_tf32x3(const float* A2, long lda2, const float* B2, long ldb2, int M, int N, int Kp, const EpiParams& p,
-                    cudaStream_t s);
+                    cudaStream_t s, long a_rows = 0, long b_rows = 0);
 // A [M, K] f32 (lda % 4 == 0, 16-byte aligned) -> A2 [M, 2 Kp] as above.
 void split_tf32(const float* A, long lda, int M, int K, float* A2, int Kp, cudaStream_t s);
 inline int tf32_kpad(int K) { return (K + 31) / 32 * 32; }

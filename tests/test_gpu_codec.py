@@ -131,6 +131,34 @@ def test_codec_bf16_tc_matches_f32(gpu, pkg, full_codec_path, B, T, lens):
         assert err < BF16_TOL, (b, err)
 
 
+@pytest.mark.parametrize("B,T,lens", [(1, 300, None), (3, 40, [40, 7, 1])])
+def test_codec_f32_tf32_matches_simt(gpu, pkg, full_codec_path, monkeypatch, B, T, lens):
+    """The fp32 decoder runs its convolutions on the tf32 hi / lo GEMM by
+    default; against its SIMT kernels (IRT_CODEC_F32_SIMT=1, read at load) on
+    the reference's random initialisation, full width, longer and ragged
+    batches than the oracle can take."""
+    g = torch.Generator().manual_seed(B * 100 + T)
+    lat = torch.randn(B, T, 32, generator=g).cuda()
+    hop = 1920
+    outs = []
+    for simt in (None, "1"):
+        if simt:
+            monkeypatch.setenv("IRT_CODEC_F32_SIMT", simt)
+        else:
+            monkeypatch.delenv("IRT_CODEC_F32_SIMT", raising=False)
+        o = torch.full((B, 1, T * hop), float("nan"), device="cuda")
+        pkg.load_codec(full_codec_path, device=0, precision="f32").decode(lat, out=o, lengths=lens)
+        torch.cuda.synchronize()
+        outs.append(o.cpu().numpy())
+    lens = lens or [T] * B
+    for b, n in enumerate(lens):
+        assert np.isfinite(outs[0][b, 0]).all()
+        assert not outs[0][b, 0, n * hop:].any()
+        err = rel_l2(outs[0][b, 0, :n * hop], outs[1][b, 0, :n * hop])
+        print(f"f32 codec tf32 vs SIMT, utt {b} len {n}: rel L2 {err:.3e}")
+        assert err < 1e-5, (b, err)
+
+
 def test_codec_weight_norm_checkpoint_resolved_at_load(gpu, pkg, synth, tmp_path):
     """A checkpoint holding the weight-norm parametrisation (X.weight_g /
     X.weight_v) decodes like the resolved one (scripts/convert_dacvae_weights.py

@@ -8,8 +8,9 @@ test calls it through the C ABI twice in a row and checks both results
 against the allocating irt_codec_decode on the same latent, at the largest
 request the fixed array holds (batch x frames = 7) and below it, for a codec
 loaded in f32 and one loaded in bf16 (the allocation-free path always runs
-the fp32 decoder, so both must match the f32 allocating decode), and that a
-request one frame larger is rejected.  The file name makes pytest
+the fp32 SIMT decoder, so both must match the f32 allocating decode on its
+SIMT kernels, IRT_CODEC_F32_SIMT=1), and that a request one frame larger is
+rejected.  The file name makes pytest
 collect it last; it also passes alone in a fresh process.
 """
 
@@ -28,12 +29,14 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-def test_decode_noalloc_matches_decode_twice(pkg, synth, tmp_path):
+def test_decode_noalloc_matches_decode_twice(pkg, synth, tmp_path, monkeypatch):
     if not torch.cuda.is_available():
         pytest.fail("CUDA device required for -m gpu tests")
     p = tmp_path / "codec_full.safetensors"
     synth.make_codec_checkpoint(str(p), seed=5, width_div=1)
+    monkeypatch.setenv("IRT_CODEC_F32_SIMT", "1")  # read at load
     codec = pkg.load_codec(str(p), device=0)
+    monkeypatch.delenv("IRT_CODEC_F32_SIMT")
     codec_bf16 = pkg.load_codec(str(p), device=0, precision="bf16")
     hop = codec.hop_length()
     g = torch.Generator().manual_seed(21)
