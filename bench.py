@@ -511,6 +511,50 @@ def cpu_model():
     return name, len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
 
 
+def tf32_case(M, reps=5):
+    """Profiling case: the fp32 mode's GEMM (tcgen05 kind::tf32 on hi / lo
+    operand halves, operands split beforehand) over the four DiT GEMM shapes of
+    one layer at M rows -- QKVG (8192 x 2048) and W13 (11776 x 2048) as f32
+    stores, Wo (2048 x 2048) and W2 (2048 x 5888) as gated residual updates --
+    timed with CUDA events on the launching stream.  Returns (per-layer ms,
+    f32-equivalent TFLOP/s = 2MNK / t; the tensor pipe runs 3x that in tf32)."""
+    import torch
+    L = ctypes.CDLL(str(PKG_DIR / "libirodori_b200_testhooks.so"))
+    L.irtt_gemm_tf32x3_async.argtypes = [ctypes.c_int] + [ctypes.c_void_p] * 2 + [ctypes.c_int] * 3 + \
+        [ctypes.c_void_p] * 2
+    L.irtt_last_error.restype = ctypes.c_char_p
+    dev = torch.device("cuda")
+    D, F = 2048, 5888
+    g = torch.Generator(device=dev).manual_seed(0)
+    shapes = [(0, 4 * D, D), (2, D, D), (0, 2 * F, D), (2, D, F)]  # (mode, N, K)
+    ops = []
+    for mode, N, K in shapes:
+        a2 = torch.randn(M, 2 * K, device=dev, generator=g)
+        b2 = torch.randn(N, 2 * K, device=dev, generator=g) * 0.02
+        out = torch.zeros(M, N, device=dev)
+        gate = torch.ones(N, device=dev)
+        ops.append((mode, a2, b2, N, K, out, gate))
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def layer():
+        for mode, a2, b2, N, K, out, gate in ops:
+            if L.irtt_gemm_tf32x3_async(mode, P(a2), P(b2), M, N, K, P(out), P(gate)):
+                raise RuntimeError(L.irtt_last_error().decode())
+
+    for _ in range(3):
+        layer()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        layer()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    flops = sum(2.0 * M * N * K for _, N, K in shapes)
+    return ms, flops / (ms / 1000.0) / 1e12
+
+
 def config1_case(pkg):
     """BASELINE config 1 run end to end, no extrapolation: the reference's
     default ModelConfig (latent 128) with random-init weights (seed 0,
@@ -675,6 +719,9 @@ def main():
                     help="only the joint attention of one layer: config-3 CFG step (c3), config-4 CFG step (c4) "
                          "or config-4 plain step (c4p); c3f / c3w: config-3 CFG step in f32 (register-tiled / "
                          "warp-per-query SIMT kernel); --steps launches (profiling case)")
+    ap.add_argument("--tf32-case", type=int, default=0,
+                    help="only the fp32 mode's tf32 hi / lo GEMM over one DiT layer's four shapes at M rows "
+                         "(profiling case)")
     ap.add_argument("--ckpt", default=None)
     ap.add_argument("--row-case", type=int, default=0,
                     help="profiling case: the adaLN modulate row kernel alone at M rows, --steps launches")
@@ -717,6 +764,12 @@ def main():
         ms, tf = attn_case(args.steps, args.attn_case)
         print(json.dumps({"attn_case": args.attn_case, "attn_case_ms": round(ms, 4), "tflops": round(tf, 1)}),
               flush=True)
+        return 0
+    if args.tf32_case:
+        load_pkg()
+        ms, tf = tf32_case(args.tf32_case, reps=args.steps)
+        print(json.dumps({"tf32_case_M": args.tf32_case, "ms_per_layer": round(ms, 4),
+                          "f32_equiv_tflops": round(tf, 1), "tf32_pipe_tflops": round(3 * tf, 1)}), flush=True)
         return 0
     if args.gemm_case:
         import torch

@@ -101,6 +101,29 @@ IRTT_API int irtt_gemm_f32(int mode, const float* A, const float* B, int M, int 
   });
 }
 
+// The tf32 hi / lo GEMM on operands already split (A2 [M, 2 Kp], B2 [N, 2 Kp]):
+// mode EPI_STORE (out = C [M, N] f32) or EPI_RESID (out = x += gate . acc), on
+// the legacy stream without synchronising (profiling loops; check with
+// irtt_sync_check()).
+IRTT_API int irtt_gemm_tf32x3_async(int mode, const float* A2, const float* B2, int M, int N, int Kp, float* out,
+                                    const float* gate) {
+  return guard([&] {
+    irt::EpiParams p;
+    p.mode = mode;
+    p.M = M;
+    p.N = N;
+    p.out_bf16 = 0;
+    if (mode == irt::EPI_RESID) {
+      p.x = out;
+      p.gate = gate;
+    } else {
+      p.out = out;
+      p.ldo = N;
+    }
+    irt::gemm_tc_tf32x3(A2, 2L * Kp, B2, 2L * Kp, M, N, Kp, p, nullptr);
+  });
+}
+
 // Fused-epilogue GEMM for the QKVG / SWIGLU / RESID modes with bf16 operands.
 IRTT_API int irtt_gemm_epi(int mode, const void* A, const void* B, int M, int N, int K, int path, void* o0, void* o1,
                            void* o2, void* o3, const float* w0, const float* w1, const float* cos_t,
