@@ -198,15 +198,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   using C = Cfg<BN, CG>;
   constexpr int STAGES = C::STAGES;
   constexpr int BMT = BM * CG;  // rows of one work tile
-  // TF: two accumulator buffers + two tile sums (see the epilogue), BN = 128
+  // TF: four 128-column accumulator buffers (see the epilogue), BN = 128
   static_assert(!TF || BN == 128, "the tf32 path runs 128-column tiles");
-  constexpr uint32_t TMEM_COLS = TF ? 4 * BN : C::TMEM_COLS;
+  constexpr int NACC = TF ? 4 : 2;
+  constexpr uint32_t TMEM_COLS = TF ? NACC * BN : C::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_EPI + C::EPI_BYTES);
   // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2]; then tmem base slot
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2 * NACC);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = CG == 2 ? cluster_rank() : 0u;
@@ -220,14 +221,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   auto full = [&](int s) { return smem_u32(&bars[s]); };
   auto empty = [&](int s) { return smem_u32(&bars[STAGES + s]); };
   auto tfull = [&](int b) { return smem_u32(&bars[2 * STAGES + b]); };
-  auto tempty = [&](int b) { return smem_u32(&bars[2 * STAGES + 2 + b]); };
+  auto tempty = [&](int b) { return smem_u32(&bars[2 * STAGES + NACC + b]); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full(s), 1);
       mbar_init(empty(s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NACC; ++b) {
       mbar_init(tfull(b), 1);
       // rank 0's accumulator-empty barrier counts the epilogue warps of the group
       mbar_init(tempty(b), EPI_WARPS * CG);
@@ -305,13 +306,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t it = 0, tl = 0;
       int t, kb0, kb1;
       if constexpr (TF) {
-        // accumulation chunks (tf_chunk_end), alternating between the two
+        // accumulation chunks (tf_chunk_end), in turn over the four
         // accumulator buffers (tl counts chunks here)
         for (int i = 0; units.get(i, t, kb0, kb1); ++i) {
           for (int c0 = kb0, c1; c0 < kb1; c0 = c1, ++tl) {
             c1 = tf_chunk_end(c0, kb1, K / 32);
-            const int buf = tl & 1;
-            const uint32_t aph = (tl >> 1) & 1;
+            const int buf = tl % NACC;
+            const uint32_t aph = (tl / NACC) & 1;
             mbar_wait(tempty(buf), aph ^ 1);
             tc_fence_after();
             const uint32_t d_tmem = tmem_base + buf * BN;
@@ -387,46 +388,51 @@ __global__ void __launch_bounds__(THREADS, 1)
       tile_coords(t, m_tiles, n_tiles, mi_, ni_);
       const int m0 = mi_ * BMT + (int)rank * BM, n0 = ni_ * BN;
       uint32_t taddr;
+      int tbuf = buf;  // the accumulator buffer this tile's epilogue reads and then releases
       if constexpr (TF) {
         const uint32_t lanes = tmem_base + ((uint32_t)(quad * 32) << 16);
         // The tensor core's f32 accumulation loses accuracy with every MMA
         // chained into one accumulator (measured relative L2 against f64: 6e-5
         // at K = 5888 in one chain; 6.5e-7 with 8-k-block chunks; 2e-7 to
         // 4.4e-7 with 2-k-block chunks).  Each chunk (tf_chunk_end) starts a
-        // fresh accumulator; these warps read it (this warp's 64 columns),
-        // hand the buffer back at once and add it into the tile sum in their
-        // registers with round-to-nearest f32 adds; the sum goes to tensor
-        // memory (sum buffer 2 + (tl & 1)) for the epilogue below.
-        const uint32_t sum = lanes + (uint32_t)(2 + (tl & 1)) * BN;
+        // fresh accumulator (four buffers in turn); these warps read it (this
+        // warp's 64 columns), hand the buffer back at once and add it into
+        // the tile sum in their registers with round-to-nearest f32 adds; the
+        // sum goes into the last chunk's buffer for the epilogue below.
         float acc[64];  // this thread's row, this warp's 64 columns of the tile sum
-        auto take = [&](bool first) {  // one chunk: into acc, then the buffer goes back
-          const int b = ch & 1;
-          mbar_wait(tfull(b), (ch >> 1) & 1);
+        // one chunk into acc; every chunk but the tile's last hands its buffer back
+        auto take = [&](bool first, bool last) {
+          const int b = ch % NACC;
+          mbar_wait(tfull(b), (ch / NACC) & 1);
           tc_fence_after();
-          uint32_t a[32];
+          uint32_t a[32], a1[32];
           tmem_ld32(lanes + b * BN, a, 64 * half);
+          tmem_ld32(lanes + b * BN, a1, 64 * half + 32);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] = first ? __uint_as_float(a[j]) : acc[j] + __uint_as_float(a[j]);
-          tmem_ld32(lanes + b * BN, a, 64 * half + 32);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            acc[32 + j] = first ? __uint_as_float(a[j]) : acc[32 + j] + __uint_as_float(a[j]);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if constexpr (CG == 2) mbar_arrive_cluster(b ? te1 : te0);
-            else mbar_arrive(tempty(b));
+          for (int j = 0; j < 32; ++j) {
+            acc[j] = first ? __uint_as_float(a[j]) : acc[j] + __uint_as_float(a[j]);
+            acc[32 + j] = first ? __uint_as_float(a1[j]) : acc[32 + j] + __uint_as_float(a1[j]);
+          }
+          if (!last) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if constexpr (CG == 2) mbar_arrive_cluster(map_rank0(tempty(b)));
+              else mbar_arrive(tempty(b));
+            }
           }
           ++ch;
+          return b;
         };
         int c1 = tf_chunk_end(kb0, kb1, K / 32);
-        take(true);
+        take(true, false);  // a tile has >= 3 chunks (one per segment at least)
         for (int c0 = c1; c0 < kb1; c0 = c1) {
           c1 = tf_chunk_end(c0, kb1, K / 32);
-          take(false);
+          tbuf = take(false, c1 >= kb1);
         }
+        // the sum goes into the last chunk's buffer, kept until the epilogue ends
+        const uint32_t sum = lanes + (uint32_t)tbuf * BN;
         {
           uint32_t o[32];
 #pragma unroll
@@ -439,8 +445,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_before();
         }
         // the sum's columns come from both warps of each lane quadrant; named
-        // barrier 1 over the epilogue warps (also orders this tile's reads of
-        // the sum before the store of the tile after next into it)
+        // barrier 1 over the epilogue warps
         asm volatile("bar.sync 1, %0;" ::"n"(32 * EPI_WARPS) : "memory");
         tc_fence_after();
         taddr = sum;
@@ -583,9 +588,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (!TF && lane == 0) {
-        if constexpr (CG == 2) mbar_arrive_cluster(buf ? te1 : te0);
-        else mbar_arrive(tempty(buf));
+      if (lane == 0) {
+        if constexpr (TF) {
+          if constexpr (CG == 2) mbar_arrive_cluster(map_rank0(tempty(tbuf)));
+          else mbar_arrive(tempty(tbuf));
+        } else {
+          if constexpr (CG == 2) mbar_arrive_cluster(buf ? te1 : te0);
+          else mbar_arrive(tempty(buf));
+        }
       }
     }
   }
