@@ -283,16 +283,22 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<KT_>::CTAS_PER_SM)
       }
       // P = 2^(s * scale - m) as packed bf16: keys 2c, 2c+1 in column c of
       // the S buffer (this thread's scores are all in registers already)
+      // (the scale-and-shift and the row sums as packed f32 pairs: the same
+      // roundings as the scalar forms, half the instructions)
       uint32_t pk[KT / 2];
-      float rs0 = 0.f, rs1 = 0.f;
+      const uint64_t sc2 = f2_pack(__float_as_uint(a.scale_log2), __float_as_uint(a.scale_log2));
+      const uint64_t nb2 = f2_pack(__float_as_uint(nbase), __float_as_uint(nbase));
+      uint64_t rs2 = 0;  // (rs0, rs1) = (+0, +0)
 #pragma unroll
       for (int c = 0; c < KT / 2; ++c) {
-        const float p0 = ex2(fmaf(__uint_as_float(sr[2 * c]), a.scale_log2, nbase));
-        const float p1 = ex2(fmaf(__uint_as_float(sr[2 * c + 1]), a.scale_log2, nbase));
-        rs0 += p0;
-        rs1 += p1;
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(sr[2 * c], sr[2 * c + 1]), sc2, nb2), x0, x1);
+        const float p0 = ex2(x0), p1 = ex2(x1);
+        rs2 = f2_add(rs2, f2_pack(__float_as_uint(p0), __float_as_uint(p1)));
         pk[c] = pack_bf16x2(p0, p1);
       }
+      float rs0, rs1;
+      f2_unpack(rs2, rs0, rs1);
 #pragma unroll
       for (int g = 0; g < KT / 64; ++g)
         tmem_st32(tmem + lane_off + TM_S + b * KT + 32 * g, *reinterpret_cast<uint32_t(*)[32]>(&pk[32 * g]));
