@@ -45,7 +45,8 @@ constexpr int TAIL_MIN_SPAN = 8;
 // MMA chain restarts at 0 and is added into the tile sum by the epilogue
 // warps); the two small-term segments (A_hi.B_lo, A_lo.B_hi, ~2^-11 of the
 // product) run one chunk each, so a chunk never adds small terms onto a large
-// accumulator.
+// accumulator.  The small-term segments come first: their long chunks keep the
+// tensor core busy while the epilogue warps finish the previous tile.
 constexpr int TF_CHUNK = 2;
 constexpr uint32_t A_BYTES = BM * BK * 2;
 
@@ -53,7 +54,7 @@ constexpr uint32_t A_BYTES = BM * BK * 2;
 // kseg k-blocks; the unit ends at kb1).
 __device__ __forceinline__ int tf_chunk_end(int c0, int kb1, int kseg) {
   const int seg_end = (c0 / kseg + 1) * kseg;
-  return min(kb1, c0 < kseg ? min(seg_end, c0 + TF_CHUNK) : seg_end);
+  return min(kb1, c0 >= 2 * kseg ? min(seg_end, c0 + TF_CHUNK) : seg_end);
 }
 
 // CG = CTAs per MMA: 1, or 2 for a CTA pair (cluster of 2) that computes a
@@ -186,8 +187,9 @@ struct Regs {
 // walks the same work units, rank 0 issues the MMAs for both.
 // TF: f32 operands as tf32 hi / lo pairs (the f32 mode).  A = [A_hi | A_lo]
 // [M, 2K] and B = [B_hi | B_lo] [N, 2K] (K a multiple of 32); the k-blocks run
-// over three segments of K / 32 blocks each -- A_hi.B_hi, A_hi.B_lo, A_lo.B_hi
-// -- into one f32 accumulator, so the product keeps about f32 accuracy
+// over three segments of K / 32 blocks each -- A_hi.B_lo, A_lo.B_hi, A_hi.B_hi
+// -- into one f32 tile sum (chunked, see the epilogue), so the product keeps
+// about f32 accuracy
 // (the dropped A_lo.B_lo term and the tf32 reading of the lo halves are
 // ~2^-22 of each product) at the tf32 tensor rate.
 template <int BN, int CG, bool TF>
@@ -281,8 +283,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             // convolution; plain GEMM: one tap, no shift)
             const int kseg = K / 32, seg = kb / kseg, kk = kb - seg * kseg;
             const int cblocks = kseg / ep.conv_taps, tap = kk / cblocks, cblk = kk - tap * cblocks;
-            ca = (seg == 2 ? cblocks * 32 : 0) + cblk * 32;
-            cb = (seg == 1 ? K : 0) + kk * 32;
+            // segments in order: A_hi.B_lo, A_lo.B_hi, A_hi.B_hi
+            ca = (seg == 1 ? cblocks * 32 : 0) + cblk * 32;
+            cb = (seg == 0 ? K : 0) + kk * 32;
             ra = m0 + tap * ep.conv_dil - ep.conv_pad;
           }
           if constexpr (CG == 2) {
