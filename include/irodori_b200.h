@@ -63,8 +63,11 @@ typedef enum irt_cfg_mode {
 } irt_cfg_mode;
 
 /* Arithmetic of the DiT / encoder path.  BF16: bf16 operands on tcgen05
- * tensor cores with f32 accumulation and an f32 residual stream.  F32: fp32
- * SIMT arithmetic throughout (parity mode). */
+ * tensor cores with f32 accumulation and an f32 residual stream.  F32 (parity
+ * mode): f32 data throughout; GEMMs of 128 or more rows on tcgen05 in tf32
+ * over hi / lo operand halves with chunked f32 accumulation (error at the
+ * level of an f32 SIMT product), the rest in fp32 SIMT arithmetic
+ * (IRT_F32_SIMT=1 in the environment at engine creation: all SIMT). */
 typedef enum irt_precision { IRT_PREC_BF16 = 0, IRT_PREC_F32 = 1 } irt_precision;
 
 /* Where the pointers of a request / output live. */
@@ -194,7 +197,10 @@ typedef struct irt_codec irt_codec;
 /* load_codec(path, device): decoder-path tensors of a weight-norm-resolved
  * DACVAE safetensors file (keys of src/codec/weights.rs:219-292).
  * precision IRT_PREC_BF16: implicit-GEMM tcgen05 convolutions (bf16 operands,
- * f32 accumulation and residual stream); IRT_PREC_F32: fp32 SIMT kernels. */
+ * f32 accumulation and residual stream); IRT_PREC_F32: f32 data, convolutions
+ * as implicit GEMMs on tcgen05 in tf32 over hi / lo operand halves with
+ * chunked f32 accumulation (IRT_CODEC_F32_SIMT=1 at creation: fp32 SIMT
+ * kernels). */
 IRT_API int irt_codec_create(int device, const char* safetensors_path, int precision, irt_codec** out);
 IRT_API int irt_codec_destroy(irt_codec* c);
 /* sample_rate() = 48000, hop_length() = 1920 (src/codec/model.rs:30-37). */
