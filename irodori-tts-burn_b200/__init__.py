@@ -326,8 +326,9 @@ class InferenceBuilder:
 
     def load_weights(self, path: str, precision: str = "bf16") -> "LoadedBuilder":
         """Load a safetensors checkpoint with ``config_json`` metadata
-        (src/inference.rs:107-116).  ``precision`` = "bf16" (tensor cores) or
-        "f32" (fp32 SIMT parity mode)."""
+        (src/inference.rs:107-116).  ``precision`` = "bf16" (bf16 tensor cores)
+        or "f32" (parity mode: f32 data, GEMMs on tf32 tensor cores over hi / lo
+        operand halves with f32-level error)."""
         if precision not in PREC:
             raise IrodoriError(22, f"unknown precision {precision!r}")
         h = ctypes.c_void_p()
@@ -602,7 +603,9 @@ def decode_noalloc(codec: DacVaeCodec, latent, wav, stream=None):
 
 
 def load_codec(path: str, device: int = 0, precision: str = "f32") -> DacVaeCodec:
-    """load_codec (src/codec/weights.rs:27-33)."""
+    """load_codec (src/codec/weights.rs:27-33).  ``precision`` = "f32" (f32 data,
+    convolutions on tf32 tensor cores over hi / lo operand halves) or "bf16"
+    (bf16 tensor-core convolutions)."""
     h = ctypes.c_void_p()
     _check(lib().irt_codec_create(device, str(path).encode(), PREC[precision], ctypes.byref(h)))
     return DacVaeCodec(h, device)
